@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Serving-scale paged decode + reshape_and_cache on B200 (sm_100a).
+
+Workload (one "step" = one layer call of the decode hot path over one batch):
+256 sequences, context lengths lognormal(median 1024, sigma 0.8) clipped to
+[16, 8192]; Qwen2.5-0.5B attention geometry (14 q heads, 2 kv heads, head_dim
+64), block_size 16, bf16; physical blocks shuffled across a pool of 1.25x
+the need; the step writes one new token per sequence through a slot mapping
+(reshape_and_cache) and runs split-K paged decode attention over the pool.
+Synthetic seeded data (no dataset or weights are involved).  Consecutive
+steps use different layers of a 4-layer pool, so every step streams ~180 MB
+of KV that is not resident in the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Under torchrun every rank runs its own 256-sequence batch on its own GPU
+(requests shard by sequence, no collective on the data path: weak scaling);
+the step time is the max over ranks.  ``--impl reference`` times the
+reference algorithm's CPU restatement (the oracle) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BATCH, MEDIAN, SIGMA, LO, HI = 256, 1024, 0.8, 16, 8192
+HQ, HKV, D, BS, SLACK, POOL_LAYERS = 14, 2, 64, 16, 1.25, 4
+METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s); decode tok/s at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def context_lengths(seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return np.clip(np.round(rng.lognormal(math.log(MEDIAN), SIGMA, BATCH)), LO, HI).astype(np.int64)
+
+
+def decode_bytes(lens: np.ndarray) -> int:
+    """Algorithmic HBM bytes of one decode launch: K+V of every context token
+    (Hkv*D*2 B each for K and for V = 512 B/token), Q in + O out (Hq*D*2 B
+    each = 3584 B/sequence), the used block-table entries and the lengths."""
+    blocks = int(np.sum(-(-lens // BS)))
+    return int(512 * lens.sum() + 3584 * len(lens) + 4 * blocks + 4 * len(lens))
+
+
+def reshape_bytes(n_tokens: int) -> int:
+    """read K+V (2*Hkv*D*2 B) + write K+V + 8 B slot = 1032 B per token."""
+    return 1032 * n_tokens
+
+
+def load_peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """Samples nvidia-smi clocks/throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = {str(g) for g in gpu_indices}
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or parts[0] not in self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (CPU restatement of the reference's algorithm)
+# ---------------------------------------------------------------------------
+def cpu_oracle_workload(seed: int):
+    from oracle import paged_attention as ora
+    rng = np.random.default_rng(seed + 7)
+    lens = context_lengths(seed)
+    need = int(np.sum(-(-lens // BS)))
+    nb = int(math.ceil(SLACK * need))
+    perm = rng.permutation(nb)
+    tables, at = [], 0
+    for n in lens:
+        k = -(-int(n) // BS)
+        tables.append(perm[at:at + k])
+        at += k
+    kc = ora.bf16_round(rng.standard_normal((1, nb, HKV, BS, D), dtype=np.float32))
+    vc = ora.bf16_round(rng.standard_normal((1, nb, HKV, BS, D), dtype=np.float32))
+    q = ora.bf16_round(rng.standard_normal((BATCH, HQ, D), dtype=np.float32))
+    return lens, tables, kc, vc, q
+
+
+def cpu_oracle_call(work, threads: int) -> float:
+    """One full 256-sequence decode layer call of the oracle; returns seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import paged_attention as ora
+    lens, tables, kc, vc, q = work
+    parts = np.array_split(np.arange(BATCH), threads)
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda idx: ora.decode_attention(q[idx], kc, vc, [tables[i] for i in idx], lens[idx], 0),
+                    [p for p in parts if len(p)]))
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(seed: int, min_seconds: float = 10.0) -> dict:
+    threads = os.cpu_count() or 1
+    work = cpu_oracle_workload(seed)
+    nbytes = decode_bytes(work[0])
+    total, calls = 0.0, 0
+    while total < min_seconds and calls < 200:
+        total += cpu_oracle_call(work, threads)
+        calls += 1
+    return {"value": round(nbytes * calls / total / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{calls} full 256-sequence decode layer calls of the numpy oracle (reference algorithm "
+                      f"restated), {total:.1f} s, {threads} threads"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    work = cpu_oracle_workload(0)
+    nbytes = decode_bytes(work[0])
+    for _ in range(args.warmup):
+        cpu_oracle_call(work, threads)
+    t = sum(cpu_oracle_call(work, threads) for _ in range(args.steps))
+    value = nbytes * args.steps / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 values, f64 math",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "serving-scale paged decode, 256 seqs, ctx lognormal(1024, 0.8) in [16, 8192], "
+                               "14q/2kv, d64, block 16", "host_threads": threads},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "one full 256-sequence decode layer call per step, numpy oracle"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def build_device_workload(seed: int, device: torch.device):
+    from pagedserve_b200 import PagedKVCache
+    rng = np.random.default_rng(seed + 7)
+    lens = context_lengths(seed)
+    need = int(np.sum(-(-lens // BS)))
+    nb = int(math.ceil(SLACK * need))
+    cache = PagedKVCache(num_blocks=nb, num_layers=POOL_LAYERS, num_kv_heads=HKV, head_dim=D, block_size=BS,
+                         dtype=torch.bfloat16, device=device, free_order=rng.permutation(nb))
+    ids = [f"seq-{i}" for i in range(BATCH)]
+    for rid, n in zip(ids, lens):
+        cache.allocate(rid, int(n))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    cache.kv_cache.k_cache.normal_(generator=gen)
+    cache.kv_cache.v_cache.normal_(generator=gen)
+    positions = [int(n) - 1 for n in lens]
+    tables = torch.from_numpy(cache.table_rows(ids)).to(device)
+    lens_t = torch.from_numpy(lens.astype(np.int32)).to(device)
+    slots = torch.tensor([cache.slot_of(r, p) for r, p in zip(ids, positions)], dtype=torch.int64, device=device)
+    q = torch.randn(BATCH, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
+    new_k = torch.randn(BATCH, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    new_v = torch.randn(BATCH, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    return dict(cache=cache, ids=ids, positions=positions, lens=lens, tables=tables, lens_t=lens_t, slots=slots,
+                q=q, new_k=new_k, new_v=new_v)
+
+
+def run_b200(args, world, rank, local):
+    from pagedserve_b200 import ops, paged_decode_attention, write_tokens
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        pg = dist
+
+    w = build_device_workload(1000 + rank, device)
+    k, v = w["cache"].kv_cache.k_cache, w["cache"].kv_cache.v_cache
+    out = torch.empty_like(w["q"])
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def reshape(layer):
+        ops.reshape_and_cache(w["new_k"], w["new_v"], k, v, w["slots"], layer, error_flag=err)
+
+    def decode(layer):
+        ops.paged_decode(w["q"], k, v, w["tables"], w["lens_t"], layer, out=out, error_flag=err)
+
+    for layer in range(POOL_LAYERS):  # warm the library, size the workspace
+        reshape(layer)
+        decode(layer)
+    torch.cuda.synchronize()
+
+    # one CUDA graph per (kernel, layer): the host enqueues a step in a few us
+    stream = torch.cuda.Stream(device)
+    g_rc, g_dec = [], []
+    with torch.cuda.stream(stream):
+        for layer in range(POOL_LAYERS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                reshape(layer)
+            g_rc.append(g)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                decode(layer)
+            g_dec.append(g)
+    torch.cuda.synchronize()
+
+    def step(s, evs=None):
+        layer = s % POOL_LAYERS
+        g_rc[layer].replay()
+        if evs is not None:
+            evs[0].record()
+        g_dec[layer].replay()
+        if evs is not None:
+            evs[1].record()
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_ids = [int(x) for x in visible.split(",")][:max(world, 1)] if visible else list(range(max(world, 1)))
+    clocks = Clocks(gpu_ids if rank == 0 else [])
+    if rank == 0:
+        clocks.__enter__()
+    barrier()
+    torch.cuda.synchronize()
+    t_start.record()
+    for s in range(args.steps):
+        step(s, dec_events[s])
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    if rank == 0:
+        clocks.__exit__(None, None, None)
+    step_ms = t_start.elapsed_time(t_end) / args.steps
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec_events)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"device error flag {int(err.item())}")
+
+    # ---- end to end through the reference-facing API, host buffers -------
+    cache, ids, positions = w["cache"], w["ids"], w["positions"]
+    q_host = w["q"].cpu().pin_memory()
+    k_host = w["new_k"].cpu().pin_memory()
+    v_host = w["new_v"].cpu().pin_memory()
+    o_host = torch.empty((BATCH, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
+    h2d_box = {}
+
+    def e2e_step(s):
+        layer = s % POOL_LAYERS
+        qd = q_host.to(device, non_blocking=True).unsqueeze(2)  # [B, Hq, 1, D]
+        kd = k_host.to(device, non_blocking=True)
+        vd = v_host.to(device, non_blocking=True)
+        write_tokens(cache, ids, positions, layer, kd, vd)
+        o = paged_decode_attention(qd, cache, ids, positions, layer)
+        o_host.copy_(o, non_blocking=True)
+
+    for s in range(min(args.warmup, 3)):
+        e2e_step(s)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e_start.record()
+    for s in range(args.steps):
+        e2e_step(s)
+    e_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+    width = cache.table_rows(ids).shape[1]
+    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + 8 * BATCH + 4 * BATCH * (width + 1)
+    d2h = o_host.numel() * 2
+
+    # ---- reduce over ranks --------------------------------------------------
+    local_stats = torch.tensor([step_ms, dec_ms, e2e_ms], dtype=torch.float64, device=device)
+    if pg is not None:
+        pg.all_reduce(local_stats, op=pg.ReduceOp.MAX)
+    step_ms, dec_ms, e2e_ms = (float(x) for x in local_stats.tolist())
+    lens = w["lens"]
+    step_bytes = decode_bytes(lens) + reshape_bytes(BATCH)
+    value = step_bytes * world / (step_ms * 1e-3) / 1e9
+    e2e_value = step_bytes * world / (e2e_ms * 1e-3) / 1e9
+    peak, peak_kind = load_peaks()
+    achieved = decode_bytes(lens) / (dec_ms * 1e-3) / 1e9
+
+    if rank == 0:
+        cpu = cpu_baseline(0) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) KV/Q, lognormal contexts)",
+            "config": {"workload": "serving-scale paged decode + reshape_and_cache: 256 seqs/GPU, ctx lognormal("
+                                   "median 1024, sigma 0.8) clipped [16, 8192], 14q/2kv heads, d64, block 16, "
+                                   "pool 1.25x need, shuffled blocks",
+                       "sum_ctx_per_gpu": int(lens.sum()), "bytes_per_step_per_gpu": step_bytes,
+                       "l2": "inputs larger than L2: 4-layer pool, consecutive steps use different layers "
+                             "(~180 MB KV each)",
+                       "launch": "CUDA graph per kernel per layer", "parallelism": f"sequence-sharded x{world}"},
+            "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
+            "pct_of_measured_peak": round(100 * value / world / peak, 2),
+            "attn_layer_tok_per_s": round(BATCH * world / (step_ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "decode_fast_kernel<bf16>", "bytes_per_launch": decode_bytes(lens),
+                         "avg_launch_ms": round(dec_ms, 5), "traffic": None},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
+                    "path": "paged_decode_attention + write_tokens (reference-facing API), pinned host buffers"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    for g in g_rc + g_dec:
+        g.reset()
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_b200(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,169 @@
+/*
+ * pagedserve_b200 - C ABI of the B200 (sm_100a) paged-attention hot path.
+ *
+ * One shared library, libpagedserve_b200.so.  Every entry point takes raw
+ * device pointers, element strides (int64), sizes (int32/int64) and a CUDA
+ * stream, returns an int status (PSB_OK or a negative PSB_ERR_*), never
+ * throws, never allocates device memory and is asynchronous on the given
+ * stream.  The caller owns every buffer.
+ *
+ * KV pool layout (unchanged from PagedServe, pagedserve/engine/kv_cache.py:10-16,51-69):
+ *     k_cache, v_cache : [num_layers, num_blocks, num_kv_heads, block_size, head_dim], contiguous
+ * so (layer, block, kv_head) is one contiguous block_size x head_dim tile.
+ *
+ * Device-detected problems (a block id outside the pool, a slot outside the
+ * pool, a context longer than its block table, an exhausted wait) never trap:
+ * the offending access is skipped and a PSB_DEVERR_* bit is OR-ed into the
+ * optional int32 word ``error_flag`` (device memory; may be NULL).
+ */
+#ifndef PAGEDSERVE_B200_H_
+#define PAGEDSERVE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* psb_stream_t;
+
+/* element types (the reference supports these three: triton_paged_decode.py:110) */
+enum { PSB_F32 = 0, PSB_F16 = 1, PSB_BF16 = 2 };
+
+/* host-side status codes */
+enum {
+  PSB_OK = 0,
+  PSB_ERR_INVALID = -1,     /* bad shape, stride, pointer or size argument */
+  PSB_ERR_WORKSPACE = -2,   /* workspace smaller than *_workspace_size() */
+  PSB_ERR_UNSUPPORTED = -3, /* geometry/dtype this build has no kernel for */
+  PSB_ERR_CUDA = -4         /* a CUDA runtime/driver call failed (see psb_last_cuda_error) */
+};
+
+/* device-side error bits written to *error_flag */
+enum {
+  PSB_DEVERR_BLOCK_RANGE = 1,   /* block id from a table outside [0, num_blocks) */
+  PSB_DEVERR_SLOT_RANGE = 2,    /* slot outside [0, num_blocks * block_size) */
+  PSB_DEVERR_CONTEXT = 4,       /* context length > table width * block_size, or < 0 */
+  PSB_DEVERR_WORKSPACE = 8,     /* split-K work exceeded the workspace */
+  PSB_DEVERR_TIMEOUT = 16,      /* an async copy / MMA wait exceeded its bound */
+  PSB_DEVERR_SEQLENS = 32       /* cu_seqlens not non-decreasing within [0, total] */
+};
+
+/* Library version string, e.g. "pagedserve_b200 0.1.0 sm_100a". */
+const char* psb_version(void);
+
+/* Text for a PSB_* status code. */
+const char* psb_status_string(int status);
+
+/* Last CUDA error code seen by the library on this thread (0 if none). */
+int psb_last_cuda_error(void);
+
+/*
+ * reshape_and_cache: slot-mapped scatter of new tokens' K/V into the pools.
+ *
+ * Replaces PagedKVCache.write_token (pagedserve/engine/paged_kv_cache.py:148-200),
+ * which the reference calls once per token per layer
+ * (pagedserve/attention/batched_paged_attention.py:115-124,
+ *  pagedserve/attention/qwen_paged_attention.py:110-119).  For token t with
+ * slot s = slot_mapping[t] (int64): block = s / block_size, offset = s % block_size,
+ *     k_cache[layer, block, h, offset, :] = key[t, h, :]   (and v likewise)
+ * bit-exactly.  A negative slot writes nothing (padding row).  key/value are
+ * [num_tokens, num_kv_heads, head_dim] with element strides (stride_t,
+ * stride_h) and unit stride along head_dim.
+ */
+int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int64_t key_stride_h, const void* value,
+                          int64_t value_stride_t, int64_t value_stride_h, void* k_cache, void* v_cache,
+                          const int64_t* slot_mapping, int32_t num_tokens, int32_t layer, int32_t num_layers,
+                          int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                          int32_t dtype, int32_t* error_flag, psb_stream_t stream);
+
+/*
+ * Workspace bytes psb_paged_decode needs for ``batch`` sequences whose
+ * contexts are at most ``max_context`` tokens (split-K partials plus one
+ * arrival counter per (sequence, kv head)).  The counter region must be zero
+ * before the first call on a workspace (psb_paged_decode_workspace_init or a
+ * memset); every call leaves it zero again.
+ */
+size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t block_size, int32_t max_context, int32_t dtype);
+
+/* Zero the counter region of a fresh workspace (async memset on ``stream``). */
+int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int32_t batch, int32_t num_kv_heads,
+                                    psb_stream_t stream);
+
+/*
+ * paged_decode: single-token GQA decode attention over the paged pool.
+ *
+ * Replaces the reference's _paged_decode_kernel launch
+ * (pagedserve/attention/triton_paged_decode.py:10-95, launched at :161-172)
+ * and, numerically, vectorized_paged_attention
+ * (pagedserve/attention/vectorized_batched_attention.py:79-159):
+ *     out[b, h, :] = softmax(scale * q[b, h, :] . K_b^T) V_b
+ * over the first context_lens[b] tokens of sequence b, read through
+ * block_tables[b, :] (int32, row stride ``table_stride`` elements); q head h
+ * reads kv head h / (q_heads / num_kv_heads).  query/out are [batch, q_heads,
+ * head_dim] with element strides (stride_b, stride_h) and unit stride along
+ * head_dim, in the pool's dtype.  Softmax and accumulation are fp32.  Long
+ * contexts are split over CTAs (split-K) and merged in the same launch by
+ * the last CTA to finish each (sequence, kv head).  ``max_context`` bounds
+ * every context_lens[b] (host-known, e.g. table width x block_size).
+ * Calls sharing one workspace must not overlap on the GPU.
+ */
+int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out, int64_t o_stride_b,
+                     int64_t o_stride_h, const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                     int64_t table_stride, const int32_t* context_lens, int32_t batch, int32_t q_heads,
+                     int32_t layer, int32_t num_layers, int64_t num_blocks, int32_t num_kv_heads,
+                     int32_t block_size, int32_t head_dim, int32_t dtype, int32_t max_context, float scale,
+                     void* workspace, size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream);
+
+/*
+ * varlen_prefill: packed ragged causal attention over freshly projected
+ * q [total, q_heads, D], k/v [total, num_kv_heads, D] (element strides
+ * (stride_t, stride_h), unit stride along D).  Sequence i owns rows
+ * cu_seqlens[i] .. cu_seqlens[i+1] and is causal within itself.
+ *
+ * Replaces the reference's one-request-at-a-time prefill attention
+ * (pagedserve/attention/qwen_paged_attention.py:121-128 calling
+ *  pagedserve/attention/paged_attention.py:10-146 with query_start_position 0).
+ * bf16/f16 with head_dim 64 run on tcgen05 tensor cores with TMEM
+ * accumulators fed by TMA; other geometries use a CUDA-core kernel.
+ */
+int psb_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                       int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, void* out,
+                       int64_t o_stride_t, int64_t o_stride_h, const int32_t* cu_seqlens, int32_t num_seqs,
+                       int32_t total_tokens, int32_t max_seqlen, int32_t q_heads, int32_t num_kv_heads,
+                       int32_t head_dim, int32_t dtype, float scale, int32_t* error_flag, psb_stream_t stream);
+
+/*
+ * pack_step: GPU-side ragged-batch packer for one engine step.
+ *
+ * Inputs (device): for each of ``batch`` scheduled requests, ``req_rows[b]``
+ * (its row in the device-resident block-table store ``table_store``
+ * [store_rows, store_width] int32), ``starts[b]`` (position of its first new
+ * token) and ``query_lens[b]`` (new tokens this step: 1 for decode, the prompt
+ * length for prefill).  Outputs (device):
+ *     cu_seqlens   [batch + 1] int32   exclusive prefix sum of query_lens
+ *     context_lens [batch]     int32   starts + query_lens  (= position + 1 for decode)
+ *     slot_mapping [total]     int64   table[pos / BS] * BS + pos % BS per new token
+ *     positions    [total]     int64   absolute position of every new token (RoPE input)
+ *     block_tables [batch, out_width] int32  the requests' table rows, zero padded
+ * ``total`` must equal sum(query_lens) (the host knows it from the step plan).
+ * Replaces the reference's host-side metadata build
+ * (pagedserve/attention/triton_paged_decode.py:134-154) and the per-token
+ * slot arithmetic of write_token (pagedserve/engine/paged_kv_cache.py:187-192).
+ */
+int psb_pack_step(const int32_t* table_store, int64_t store_width, int32_t store_rows, const int32_t* req_rows,
+                  const int32_t* starts, const int32_t* query_lens, int32_t batch, int32_t total, int32_t block_size,
+                  int32_t* cu_seqlens, int32_t* context_lens, int64_t* slot_mapping, int64_t* positions,
+                  int32_t* block_tables, int32_t out_width, int32_t* error_flag, psb_stream_t stream);
+
+/* Number of SMs of the current device (for callers sizing persistent grids). */
+int psb_device_sm_count(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* PAGEDSERVE_B200_H_ */

@@ -1,0 +1,20 @@
+"""pagedserve_b200: PagedServe's paged-attention hot path for NVIDIA B200 (sm_100a).
+
+Public surface:
+
+* ``paged_decode_attention`` - drop-in for ``triton_paged_decode_attention``
+  (pagedserve/attention/triton_paged_decode.py:98)
+* ``write_tokens`` - batched replacement of the per-row ``write_token`` loop
+* ``ops.reshape_and_cache / paged_decode / varlen_prefill / pack_step`` -
+  tensor-level API over the C ABI (include/pagedserve_b200.h)
+* ``PagedKVCache`` and friends - host-side block bookkeeping with the
+  reference's interface
+"""
+
+from . import ops
+from .attention import paged_decode_attention, write_tokens
+from .paged_kv import BlockManager, BlockTable, KVCache, PagedKVCache
+
+__all__ = ["ops", "paged_decode_attention", "write_tokens", "BlockManager", "BlockTable", "KVCache",
+           "PagedKVCache"]
+__version__ = "0.1.0"

@@ -1,0 +1,92 @@
+"""ctypes binding of libpagedserve_b200.so (the C ABI in include/pagedserve_b200.h).
+
+The library is built in-tree by ``python -m pagedserve_b200.build``.  There is
+no fallback: if the library is missing or fails to load, every entry point
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpagedserve_b200.so")
+
+PSB_F32, PSB_F16, PSB_BF16 = 0, 1, 2
+PSB_OK, PSB_ERR_INVALID, PSB_ERR_WORKSPACE, PSB_ERR_UNSUPPORTED, PSB_ERR_CUDA = 0, -1, -2, -3, -4
+
+DEVERR_BITS = {
+    1: "block id outside the pool",
+    2: "slot outside the pool",
+    4: "context length outside the block table",
+    8: "split-K work exceeded the workspace",
+    16: "async wait exceeded its bound",
+    32: "cu_seqlens malformed",
+}
+
+_c_void_p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/pagedserve_b200.h
+SIGNATURES = {
+    "psb_version": (ctypes.c_char_p, []),
+    "psb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "psb_last_cuda_error": (ctypes.c_int, []),
+    "psb_device_sm_count": (ctypes.c_int, []),
+    "psb_reshape_and_cache": (ctypes.c_int, [
+        _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i64,
+        _i32, _i32, _i32, _i32, _c_void_p, _c_void_p]),
+    "psb_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
+    "psb_paged_decode_workspace_init": (ctypes.c_int, [_c_void_p, _sz, _i32, _i32, _c_void_p]),
+    "psb_paged_decode": (ctypes.c_int, [
+        _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32,
+        _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p, _sz, _c_void_p, _c_void_p]),
+    "psb_varlen_prefill": (ctypes.c_int, [
+        _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p,
+        _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p, _c_void_p]),
+    "psb_pack_step": (ctypes.c_int, [
+        _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p,
+        _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and declare every entry point's signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing; build it with `python -m pagedserve_b200.build` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status == PSB_OK:
+        return
+    lib = load()
+    msg = lib.psb_status_string(status).decode()
+    if status == PSB_ERR_CUDA:
+        msg += f" (cuda error {lib.psb_last_cuda_error()})"
+    raise NativeError(f"{what} failed: {msg} [{status}]")
+
+
+def describe_device_error(bits: int) -> str:
+    return ", ".join(text for bit, text in DEVERR_BITS.items() if bits & bit) or "none"

@@ -1,0 +1,117 @@
+"""Reference-facing attention entry points (the drop-in boundary).
+
+``paged_decode_attention`` has exactly the signature, argument meaning and
+``ValueError`` conditions/messages of the reference's Triton wrapper
+``triton_paged_decode_attention`` (pagedserve/attention/triton_paged_decode.py:98-173),
+so PagedServe's decode glue can call it in place of the Triton kernel:
+
+    pagedserve.attention.batched_paged_attention.triton_paged_decode_attention = paged_decode_attention
+
+Differences are internal: the per-row host loop that builds the padded table
+is one numpy pass and one host->device copy of (table, lengths), and the
+attention runs in the sm_100a split-K kernel of ``libpagedserve_b200.so``.
+``write_tokens`` replaces the per-row ``write_token`` loop
+(pagedserve/attention/batched_paged_attention.py:115-124) with one
+``reshape_and_cache`` launch.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import numpy as np
+import torch
+
+from . import ops
+
+
+def _host_metadata(cache, request_ids, positions, device):
+    """(table [B, M] int32, lengths [B] int32) as one device tensor pair.
+
+    Raises the reference's position error (triton_paged_decode.py:134-141).
+    """
+    lengths = np.empty(len(request_ids), dtype=np.int32)
+    tables = []
+    for row, (rid, pos) in enumerate(zip(request_ids, positions)):
+        count = cache.token_count(rid)
+        if not 0 <= pos < count:
+            raise ValueError(f"Invalid position {pos} for {rid}")
+        lengths[row] = pos + 1
+        tables.append(cache.get_block_table(rid).get_blocks())
+    width = max(len(t) for t in tables)
+    packed = np.zeros((len(tables), width + 1), dtype=np.int32)  # [table | length]
+    for row, t in enumerate(tables):
+        packed[row, : len(t)] = t
+    packed[:, width] = lengths
+    host = torch.from_numpy(packed)
+    if device.type == "cuda":
+        host = host.pin_memory()
+    dev = host.to(device, non_blocking=True)
+    return dev[:, :width], dev[:, width].contiguous(), width
+
+
+def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str], positions: Sequence[int],
+                           layer: int) -> torch.Tensor:
+    """Decode attention for query ``[B, Hq, 1, D]``, returning the same shape.
+
+    Drop-in for ``triton_paged_decode_attention`` (triton_paged_decode.py:98-104).
+    """
+    if not query.is_cuda:
+        raise ValueError("B200 paged attention requires CUDA")
+    if query.ndim != 4 or query.shape[2] != 1:
+        raise ValueError("query must have shape [B, Hq, 1, D]")
+    if query.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise ValueError("Unsupported query dtype")
+    batch, q_heads, _, head_dim = query.shape
+    kv = cache.kv_cache
+    kv_heads = kv.num_kv_heads
+    if batch == 0:
+        raise ValueError("Batch must not be empty")
+    if len(request_ids) != batch or len(positions) != batch:
+        raise ValueError("Request IDs and positions must match batch size")
+    if len(set(request_ids)) != batch:
+        raise ValueError("Request IDs must be unique")
+    if head_dim != kv.head_dim:
+        raise ValueError("Head dimension mismatch")
+    if q_heads % kv_heads:
+        raise ValueError("Query heads must be divisible by KV heads")
+    if query.dtype != kv.dtype:
+        raise ValueError("Query dtype must match cache dtype")
+    if query.device != kv.k_cache.device:
+        raise ValueError("Query and cache must be on the same device")
+    if not 0 <= layer < kv.k_cache.shape[0]:
+        raise ValueError("Invalid layer")
+    tables, lengths, width = _host_metadata(cache, request_ids, positions, query.device)
+    return ops.paged_decode(query, kv.k_cache, kv.v_cache, tables, lengths, layer,
+                            max_context=width * cache.block_size)
+
+
+def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], layer: int, key: torch.Tensor,
+                 value: torch.Tensor) -> None:
+    """Write row ``b``'s ``key[b], value[b] [Hkv, D]`` at ``positions[b]`` of
+    ``request_ids[b]``, for every row in one launch.
+
+    Same validation as ``PagedKVCache.write_token`` (paged_kv_cache.py:158-185)
+    per row, same bytes written (paged_kv_cache.py:187-200).
+    """
+    kv = cache.kv_cache
+    if key.ndim == 4:  # [B, Hkv, 1, D] as produced by the decode glue
+        key, value = key.squeeze(2), value.squeeze(2)
+    shape = (kv.num_kv_heads, kv.head_dim)
+    if tuple(key.shape[1:]) != shape or tuple(value.shape[1:]) != shape:
+        raise ValueError(f"Expected K/V shape {shape}; got key={tuple(key.shape)}, value={tuple(value.shape)}")
+    if key.dtype != kv.dtype or value.dtype != kv.dtype:
+        raise ValueError(f"K/V tensors must have dtype {kv.dtype}")
+    slots = np.fromiter((cache.slot_of(r, p) if hasattr(cache, "slot_of") else _slot(cache, r, p)
+                         for r, p in zip(request_ids, positions)), dtype=np.int64, count=len(request_ids))
+    slot_t = torch.from_numpy(slots).to(key.device, non_blocking=True)
+    ops.reshape_and_cache(key, value, kv.k_cache, kv.v_cache, slot_t, layer)
+
+
+def _slot(cache, request_id: str, position: int) -> int:
+    """Slot of a position for a reference ``PagedKVCache`` (paged_kv_cache.py:187-192)."""
+    count = cache.token_count(request_id)
+    if not 0 <= position < count:
+        raise IndexError(f"Invalid token position: {position}; valid range is [0, {count})")
+    bs = cache.block_size
+    return cache.get_block_table(request_id).get_physical_block(position // bs) * bs + position % bs

@@ -1,0 +1,142 @@
+// Host-side helpers: device properties, occupancy, error bookkeeping and TMA
+// tensor-map encoding through the driver entry point (no -lcuda needed).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/pagedserve_b200.h"
+#include "host_util.h"
+
+namespace psb {
+namespace {
+thread_local int g_last_cuda_error = 0;
+std::mutex g_mu;
+std::unordered_map<int, int> g_sm_count;
+std::unordered_map<uint64_t, int> g_occ;  // (device, func, smem) -> occupancy
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+int record_cuda_error(cudaError_t e) {
+  g_last_cuda_error = static_cast<int>(e);
+  return PSB_ERR_CUDA;
+}
+
+int check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PSB_OK : record_cuda_error(e);
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_sm_count.find(dev);
+  if (it != g_sm_count.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  g_sm_count[dev] = n;
+  return n;
+}
+
+bool kernel_occupancy(const void* func, int threads, size_t smem, int* blocks_per_sm) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t key = (static_cast<uint64_t>(dev) << 56) ^ (reinterpret_cast<uint64_t>(func) << 20) ^
+                       (static_cast<uint64_t>(smem) << 2) ^ static_cast<uint64_t>(threads);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) {
+      *blocks_per_sm = it->second;
+      return true;
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return record_cuda_error(e), false;
+  int n = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem);
+  if (e != cudaSuccess) return record_cuda_error(e), false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_occ[key] = n;
+  *blocks_per_sm = n;
+  return true;
+}
+
+CUtensorMapDataType dtype_to_tmap(int dtype) {
+  switch (dtype) {
+    case PSB_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case PSB_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int block_size, int head_dim,
+                          CUtensorMapDataType dt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const size_t esz = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(block_size),
+                              static_cast<cuuint64_t>(tiles)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * esz),
+                                 static_cast<cuuint64_t>(head_dim * esz * block_size)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(block_size), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = 10000 + static_cast<int>(r);
+    return false;
+  }
+  return true;
+}
+
+bool encode_matrix_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+                       int box_rows, int box_cols, CUtensorMapDataType dt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const size_t esz = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems * esz)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = 10000 + static_cast<int>(r);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace psb
+
+extern "C" const char* psb_version(void) { return "pagedserve_b200 0.1.0 sm_100a"; }
+
+extern "C" const char* psb_status_string(int status) {
+  switch (status) {
+    case PSB_OK: return "ok";
+    case PSB_ERR_INVALID: return "invalid argument";
+    case PSB_ERR_WORKSPACE: return "workspace too small";
+    case PSB_ERR_UNSUPPORTED: return "unsupported geometry or dtype";
+    case PSB_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int psb_last_cuda_error(void) { return psb::g_last_cuda_error; }
+
+extern "C" int psb_device_sm_count(void) { return psb::device_sm_count(); }

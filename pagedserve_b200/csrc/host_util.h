@@ -1,0 +1,39 @@
+// Host-side helpers shared by the pagedserve_b200 translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace psb {
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// SM count of the current device (cached per device).
+int device_sm_count();
+
+// Max resident CTAs per SM for ``func`` at ``threads`` and ``smem`` dynamic
+// bytes; raises the kernel's dynamic shared-memory limit when needed.
+bool kernel_occupancy(const void* func, int threads, size_t smem, int* blocks_per_sm);
+
+// Remember a CUDA error for psb_last_cuda_error(); returns PSB_ERR_CUDA.
+int record_cuda_error(cudaError_t e);
+
+// PSB_OK, or PSB_ERR_CUDA when the last launch failed.
+int check_launch();
+
+CUtensorMapDataType dtype_to_tmap(int dtype);
+
+// 3-D tiled map over a paged pool viewed as [tiles, block_size, head_dim]
+// (one tile per (layer, block, kv head)), box = one whole tile, 128-byte
+// swizzle.  head_dim * element size must be 128 bytes.
+bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int block_size, int head_dim,
+                          CUtensorMapDataType dt);
+
+// 2-D tiled map over a row-major [rows, cols] matrix with row pitch
+// ``row_stride_elems``; box = box_rows x box_cols, 128-byte swizzle.
+bool encode_matrix_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+                       int box_rows, int box_cols, CUtensorMapDataType dt);
+
+}  // namespace psb

@@ -1,0 +1,242 @@
+"""Tensor-level API over the C ABI: the batched hot path the engine calls.
+
+* ``reshape_and_cache``  one launch per layer for all new tokens (replaces the
+  per-token ``PagedKVCache.write_token`` loop,
+  pagedserve/attention/batched_paged_attention.py:115-124)
+* ``paged_decode``       split-K GQA decode over the paged pool (replaces
+  pagedserve/attention/triton_paged_decode.py:10-95)
+* ``varlen_prefill``     packed ragged causal prefill (replaces the per-request
+  prefill of pagedserve/attention/qwen_paged_attention.py:121-128)
+* ``pack_step``          GPU-side ragged-batch metadata for one engine step
+  (replaces pagedserve/attention/triton_paged_decode.py:134-154)
+
+Every function requires CUDA tensors, launches on the current stream and
+returns without synchronising.  There is no CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _native
+
+_DTYPES = {torch.float32: _native.PSB_F32, torch.float16: _native.PSB_F16, torch.bfloat16: _native.PSB_BF16}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise ValueError(f"Unsupported dtype {dtype}") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("B200 paged attention requires CUDA tensors")
+
+
+def _pool_geometry(k_cache: torch.Tensor, v_cache: torch.Tensor):
+    if k_cache.ndim != 5 or v_cache.shape != k_cache.shape:
+        raise ValueError("k_cache/v_cache must be [num_layers, num_blocks, num_kv_heads, block_size, head_dim]")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("KV pools must be contiguous")
+    if k_cache.dtype != v_cache.dtype:
+        raise ValueError("k_cache and v_cache dtypes differ")
+    return tuple(int(x) for x in k_cache.shape)
+
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      slot_mapping: torch.Tensor, layer: int, error_flag: torch.Tensor | None = None) -> None:
+    """Scatter ``key, value [T, Hkv, D]`` into ``k_cache/v_cache[layer]`` at ``slot_mapping [T]`` (int64).
+
+    Bit-exact with ``PagedKVCache.write_token`` (paged_kv_cache.py:187-200); a
+    negative slot writes nothing.
+    """
+    _require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    nl, nb, hkv, bs, d = _pool_geometry(k_cache, v_cache)
+    if key.ndim != 3 or key.shape[1:] != (hkv, d) or value.shape != key.shape:
+        raise ValueError(f"key/value must be [T, {hkv}, {d}]")
+    if key.dtype != k_cache.dtype or value.dtype != k_cache.dtype:
+        raise ValueError("key/value dtype must match the cache dtype")
+    if key.stride(2) != 1 or value.stride(2) != 1:
+        raise ValueError("key/value need unit stride along head_dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.ndim != 1 or slot_mapping.shape[0] != key.shape[0]:
+        raise ValueError("slot_mapping must be int64 [T]")
+    if not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.contiguous()
+    if not 0 <= layer < nl:
+        raise ValueError("Invalid layer")
+    lib = _native.load()
+    _native.check(lib.psb_reshape_and_cache(
+        key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(), value.stride(0), value.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(), key.shape[0], layer, nl, nb, hkv, bs, d,
+        dtype_code(k_cache.dtype), _ptr(error_flag), _stream(key.device)), "reshape_and_cache")
+
+
+class DecodeWorkspace:
+    """Split-K scratch for ``paged_decode``: one growable buffer per device.
+
+    The first bytes hold per-(sequence, kv head) arrival counters that must be
+    zero before a launch; every launch leaves them zero, so the buffer is
+    zeroed only when it is (re)allocated.  Launches sharing a workspace must be
+    ordered (same stream), which is what the per-device default gives.
+    """
+
+    _lock = threading.Lock()
+    _per_device: dict[int, "DecodeWorkspace"] = {}
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.buffer = torch.empty(0, dtype=torch.uint8, device=device)
+
+    @classmethod
+    def for_device(cls, device: torch.device) -> "DecodeWorkspace":
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        with cls._lock:
+            ws = cls._per_device.get(idx)
+            if ws is None:
+                ws = cls._per_device[idx] = DecodeWorkspace(torch.device("cuda", idx))
+            return ws
+
+    def get(self, nbytes: int, batch: int, hkv: int) -> torch.Tensor:
+        if self.buffer.numel() < nbytes:
+            self.buffer = torch.empty(max(nbytes, 2 * self.buffer.numel()), dtype=torch.uint8, device=self.device)
+            lib = _native.load()
+            # zero the whole buffer once: covers the counters of any later, larger batch too
+            self.buffer.zero_()
+        return self.buffer
+
+
+def decode_workspace_bytes(batch: int, q_heads: int, hkv: int, head_dim: int, block_size: int, max_context: int,
+                           dtype: torch.dtype) -> int:
+    lib = _native.load()
+    return int(lib.psb_paged_decode_workspace_size(batch, q_heads, hkv, head_dim, block_size, max_context,
+                                                   dtype_code(dtype)))
+
+
+def paged_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                 context_lens: torch.Tensor, layer: int, scale: float | None = None, out: torch.Tensor | None = None,
+                 max_context: int | None = None, workspace: torch.Tensor | None = None,
+                 error_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention for ``query [B, Hq, D]`` (or ``[B, Hq, 1, D]``) over the paged pool.
+
+    ``block_tables [B, M]`` int32 and ``context_lens [B]`` int32 live on the
+    device; ``max_context`` (default ``M * block_size``) bounds every length.
+    Returns ``out`` with ``query``'s shape and dtype.
+    """
+    _require_cuda(query, k_cache, v_cache, block_tables, context_lens)
+    nl, nb, hkv, bs, d = _pool_geometry(k_cache, v_cache)
+    q3 = query.squeeze(2) if query.ndim == 4 else query
+    if q3.ndim != 3 or q3.shape[2] != d:
+        raise ValueError("query must be [B, Hq, D] or [B, Hq, 1, D]")
+    bsz, hq, _ = q3.shape
+    if bsz == 0:
+        raise ValueError("Batch must not be empty")
+    if hq % hkv:
+        raise ValueError("Query heads must be divisible by KV heads")
+    if q3.dtype != k_cache.dtype:
+        raise ValueError("Query dtype must match cache dtype")
+    if q3.stride(2) != 1:
+        q3 = q3.contiguous()
+    if block_tables.dtype != torch.int32 or block_tables.ndim != 2 or block_tables.shape[0] != bsz:
+        raise ValueError("block_tables must be int32 [B, max_blocks]")
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    if context_lens.dtype != torch.int32 or context_lens.shape != (bsz,):
+        raise ValueError("context_lens must be int32 [B]")
+    context_lens = context_lens.contiguous()
+    if not 0 <= layer < nl:
+        raise ValueError("Invalid layer")
+    if max_context is None:
+        max_context = block_tables.shape[1] * bs
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    if out is None:
+        out = torch.empty_like(query)
+    o3 = out.squeeze(2) if out.ndim == 4 else out
+    if o3.shape != q3.shape or o3.stride(2) != 1 or o3.dtype != q3.dtype:
+        raise ValueError("out must match query's shape/dtype with unit stride along head_dim")
+    need = decode_workspace_bytes(bsz, hq, hkv, d, bs, max_context, q3.dtype)
+    if workspace is None:
+        workspace = DecodeWorkspace.for_device(query.device).get(need, bsz, hkv)
+    lib = _native.load()
+    _native.check(lib.psb_paged_decode(
+        q3.data_ptr(), q3.stride(0), q3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1), k_cache.data_ptr(),
+        v_cache.data_ptr(), block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), bsz, hq, layer,
+        nl, nb, hkv, bs, d, dtype_code(q3.dtype), int(max_context), scale, workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _ptr(error_flag), _stream(query.device)), "paged_decode")
+    return out
+
+
+def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,
+                   scale: float | None = None, out: torch.Tensor | None = None,
+                   error_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed causal prefill: ``q [T, Hq, D]``, ``k, v [T, Hkv, D]``, ``cu_seqlens [B+1]`` int32."""
+    _require_cuda(q, k, v, cu_seqlens)
+    if q.ndim != 3 or k.ndim != 3 or v.shape != k.shape or q.shape[0] != k.shape[0] or q.shape[2] != k.shape[2]:
+        raise ValueError("q must be [T, Hq, D] and k, v [T, Hkv, D]")
+    t, hq, d = q.shape
+    hkv = k.shape[1]
+    if hq % hkv:
+        raise ValueError("Query heads must be divisible by KV heads")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v dtypes differ")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.ndim != 1 or cu_seqlens.shape[0] < 1:
+        raise ValueError("cu_seqlens must be int32 [B+1]")
+    q, k, v = (x if x.stride(2) == 1 else x.contiguous() for x in (q, k, v))
+    cu_seqlens = cu_seqlens.contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    if out.shape != q.shape or out.stride(2) != 1:
+        raise ValueError("out must match q with unit stride along head_dim")
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    lib = _native.load()
+    _native.check(lib.psb_varlen_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(), v.stride(0),
+        v.stride(1), out.data_ptr(), out.stride(0), out.stride(1), cu_seqlens.data_ptr(), cu_seqlens.shape[0] - 1,
+        t, int(max_seqlen), hq, hkv, d, dtype_code(q.dtype), scale, _ptr(error_flag), _stream(q.device)),
+        "varlen_prefill")
+    return out
+
+
+def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.Tensor, query_lens: torch.Tensor,
+              total: int, block_size: int, out_width: int | None = None, error_flag: torch.Tensor | None = None):
+    """Build one step's ragged-batch metadata on the GPU.
+
+    ``table_store [R, W]`` int32 holds every live request's block table (one
+    row each); ``req_rows, starts, query_lens [B]`` int32 are the scheduler's
+    step plan.  Returns ``(cu_seqlens, context_lens, slot_mapping, positions,
+    block_tables)``.
+    """
+    _require_cuda(table_store, req_rows, starts, query_lens)
+    for name, x in (("req_rows", req_rows), ("starts", starts), ("query_lens", query_lens)):
+        if x.dtype != torch.int32 or x.ndim != 1:
+            raise ValueError(f"{name} must be int32 [B]")
+    if table_store.dtype != torch.int32 or table_store.ndim != 2 or table_store.stride(1) != 1:
+        raise ValueError("table_store must be int32 [R, W] with unit column stride")
+    bsz = req_rows.shape[0]
+    out_width = table_store.shape[1] if out_width is None else int(out_width)
+    dev = table_store.device
+    cu = torch.empty(bsz + 1, dtype=torch.int32, device=dev)
+    ctx = torch.empty(bsz, dtype=torch.int32, device=dev)
+    slots = torch.empty(total, dtype=torch.int64, device=dev)
+    pos = torch.empty(total, dtype=torch.int64, device=dev)
+    tables = torch.empty((bsz, out_width), dtype=torch.int32, device=dev)
+    lib = _native.load()
+    _native.check(lib.psb_pack_step(
+        table_store.data_ptr(), table_store.stride(0), table_store.shape[0], req_rows.contiguous().data_ptr(),
+        starts.contiguous().data_ptr(), query_lens.contiguous().data_ptr(), bsz, int(total), int(block_size),
+        cu.data_ptr(), ctx.data_ptr(), slots.data_ptr(), pos.data_ptr(), tables.data_ptr(), out_width,
+        _ptr(error_flag), _stream(dev)), "pack_step")
+    return cu, ctx, slots, pos, tables
