@@ -23,6 +23,10 @@ int record_cuda_error(cudaError_t e);
 // PSB_OK, or PSB_ERR_CUDA when the last launch failed.
 int check_launch();
 
+// Drop a non-sticky error another library left in this thread's runtime
+// state, so check_launch() reports only our own launch.
+inline void discard_stale_error() { (void)cudaGetLastError(); }
+
 CUtensorMapDataType dtype_to_tmap(int dtype);
 
 // 3-D tiled map over a paged pool viewed as [tiles, block_size, head_dim]

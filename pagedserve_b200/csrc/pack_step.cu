@@ -129,6 +129,7 @@ extern "C" int psb_pack_step(const int32_t* table_store, int64_t store_width, in
   if (!kernel_occupancy(reinterpret_cast<const void*>(pack_step_kernel), kPackThreads, smem, &occ)) return PSB_ERR_CUDA;
   const int64_t work = std::max<int64_t>(total, static_cast<int64_t>(batch) * out_width);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((work + kPackThreads - 1) / kPackThreads, sms));
+  discard_stale_error();
   pack_step_kernel<<<static_cast<unsigned>(grid), kPackThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       table_store, store_width, store_rows, req_rows, starts, query_lens, batch, total, block_size, cu_seqlens,
       context_lens, slot_mapping, positions, block_tables, out_width, error_flag);

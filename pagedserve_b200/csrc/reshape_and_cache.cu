@@ -83,14 +83,17 @@ extern "C" int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int6
   char* kc = static_cast<char*>(k_cache);
   char* vc = static_cast<char*>(v_cache);
   if (vec16) {
+    discard_stale_error();
     reshape_and_cache_kernel<uint4><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
         kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
         row_bytes, pool_slots, error_flag);
   } else if (esz == 4) {
+    discard_stale_error();
     reshape_and_cache_kernel<uint32_t><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
         kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
         row_bytes, pool_slots, error_flag);
   } else {
+    discard_stale_error();
     reshape_and_cache_kernel<uint16_t><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
         kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
         row_bytes, pool_slots, error_flag);

@@ -98,6 +98,7 @@ int launch_generic(const PrefillParams& p, cudaStream_t s) {
   if (blocks == 0) return PSB_OK;
   if (blocks >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
   const size_t smem = sizeof(float) * (kGenThreads / 32) * p.head_dim;
+  discard_stale_error();
   prefill_generic_kernel<T><<<static_cast<unsigned>(blocks), kGenThreads, smem, s>>>(p);
   return check_launch();
 }
@@ -152,6 +153,7 @@ extern "C" int psb_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_s
   p.err = error_flag;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (error_flag != nullptr) {
+    discard_stale_error();
     check_seqlens_kernel<<<1, 256, 0, s>>>(cu_seqlens, num_seqs, total_tokens, error_flag);
   }
   if (prefill_tc_supported(p, dtype)) return prefill_tc_launch(p, dtype, s);

@@ -191,8 +191,10 @@ def test_strided_query_and_output_like_projection_layout():
     c = _synthetic(17, [20, 300, 700])
     kc, vc = poison_unused(c["k_cache"], c["v_cache"], c["layer"], c["tables"], c["context_lens"])
     k, v = to_dev(kc, "bfloat16"), to_dev(vc, "bfloat16")
-    flat = to_dev(c["q"].reshape(3, 1, 14 * 64), "bfloat16")
-    q = flat.view(3, 1, 14, 64).transpose(1, 2)  # [B, Hq, 1, D], non-contiguous
+    # a fused QKV projection output: q is a strided view of [B, (14 + 2 + 2) * 64]
+    qkv = torch.zeros(3, 18 * 64, device="cuda", dtype=torch.bfloat16)
+    qkv[:, : 14 * 64] = to_dev(c["q"].reshape(3, 14 * 64), "bfloat16")
+    q = qkv[:, : 14 * 64].view(3, 14, 1, 64)  # [B, Hq, 1, D], row stride 1152
     assert not q.is_contiguous()
     table = torch.from_numpy(ora.padded_block_table(c["tables"])).cuda()
     lens = torch.tensor(c["context_lens"], dtype=torch.int32, device="cuda")

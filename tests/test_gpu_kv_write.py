@@ -55,7 +55,8 @@ def test_reshape_and_cache_reproduces_reference_pools(dtype):
 def test_reshape_and_cache_bit_exact_random(dtype, hkv, d, bs):
     from pagedserve_b200 import ops
     rng = np.random.default_rng(hkv * 1000 + d + bs)
-    layers, nb, t = 3, 64, 300
+    layers, nb = 3, 64
+    t = min(300, nb * bs)
     pool_k = rng.standard_normal((layers, nb, hkv, bs, d), dtype=np.float32)
     pool_v = rng.standard_normal((layers, nb, hkv, bs, d), dtype=np.float32)
     if dtype != "float32":
