@@ -2,8 +2,12 @@
 // tensor-map encoding through the driver entry point (no -lcuda needed).
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <unordered_map>
+#include <utility>
 
 #include "../../include/pagedserve_b200.h"
 #include "host_util.h"
@@ -13,7 +17,8 @@ namespace {
 thread_local int g_last_cuda_error = 0;
 std::mutex g_mu;
 std::unordered_map<int, int> g_sm_count;
-std::unordered_map<uint64_t, int> g_occ;  // (device, func, smem) -> occupancy
+std::map<std::tuple<int, uintptr_t, size_t, int>, int> g_occ;  // (device, func, smem, threads) -> CTAs/SM
+std::set<std::pair<int, uintptr_t>> g_smem_raised;             // (device, func) with the smem ceiling raised
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
@@ -53,23 +58,34 @@ int device_sm_count() {
 bool kernel_occupancy(const void* func, int threads, size_t smem, int* blocks_per_sm) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const uint64_t key = (static_cast<uint64_t>(dev) << 56) ^ (reinterpret_cast<uint64_t>(func) << 20) ^
-                       (static_cast<uint64_t>(smem) << 2) ^ static_cast<uint64_t>(threads);
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    auto it = g_occ.find(key);
-    if (it != g_occ.end()) {
-      *blocks_per_sm = it->second;
-      return true;
+  const auto fkey = std::make_pair(dev, reinterpret_cast<uintptr_t>(func));
+  const auto okey = std::make_tuple(dev, reinterpret_cast<uintptr_t>(func), smem, threads);
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_occ.find(okey);
+  if (it != g_occ.end()) {
+    *blocks_per_sm = it->second;
+    return true;
+  }
+  // Raise the kernel's dynamic shared-memory ceiling once, to the device
+  // maximum, so launches with any smaller size stay valid afterwards.
+  if (g_smem_raised.insert(fkey).second) {
+    int optin = 0;
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, func);
+    // the ceiling is the opt-in maximum less the kernel's static shared memory
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               optin - static_cast<int>(fa.sharedSizeBytes));
+    if (e != cudaSuccess) {
+      g_smem_raised.erase(fkey);
+      return record_cuda_error(e), false;
     }
   }
-  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return record_cuda_error(e), false;
   int n = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem);
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem);
   if (e != cudaSuccess) return record_cuda_error(e), false;
-  std::lock_guard<std::mutex> lk(g_mu);
-  g_occ[key] = n;
+  g_occ[okey] = n;
   *blocks_per_sm = n;
   return true;
 }
