@@ -103,16 +103,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// Same, but a thread whose phase is still open sleeps up to ``hint_ns``
+// (it wakes as soon as the phase completes) instead of returning at once.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase ``parity`` of ``bar`` to complete; false when the wall-time
 // bound expired first (the caller records the timeout and unwinds).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
+  if (mbar_try_wait_sleep(addr, parity, 100000u)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait_sleep(addr, parity, 100000u)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
+}
+
+// Global atomic add with acquire-release semantics at GPU scope.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
 }
 
 // ---------------------------------------------------------------------------

@@ -99,7 +99,7 @@ CUtensorMapDataType dtype_to_tmap(int dtype) {
 }
 
 bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int block_size, int head_dim,
-                          CUtensorMapDataType dt) {
+                          int box_tiles, CUtensorMapDataType dt) {
   auto fn = encode_fn();
   if (!fn) return false;
   const size_t esz = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
@@ -107,7 +107,8 @@ bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int
                               static_cast<cuuint64_t>(tiles)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * esz),
                                  static_cast<cuuint64_t>(head_dim * esz * block_size)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(block_size), 1};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(block_size),
+                             static_cast<cuuint32_t>(box_tiles)};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = fn(map, dt, 3, const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -30,10 +30,10 @@ inline void discard_stale_error() { (void)cudaGetLastError(); }
 CUtensorMapDataType dtype_to_tmap(int dtype);
 
 // 3-D tiled map over a paged pool viewed as [tiles, block_size, head_dim]
-// (one tile per (layer, block, kv head)), box = one whole tile, 128-byte
-// swizzle.  head_dim * element size must be 128 bytes.
+// (one tile per (layer, block, kv head)), box = ``box_tiles`` whole
+// consecutive tiles, 128-byte swizzle.  head_dim * element size must be 128 bytes.
 bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int block_size, int head_dim,
-                          CUtensorMapDataType dt);
+                          int box_tiles, CUtensorMapDataType dt);
 
 // 2-D tiled map over a row-major [rows, cols] matrix with row pitch
 // ``row_stride_elems``; box = box_rows x box_cols, 128-byte swizzle.
