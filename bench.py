@@ -264,40 +264,34 @@ def run_b200(args, world, rank, local):
         decode(layer)
     torch.cuda.synchronize()
 
-    # one CUDA graph per (kernel, layer): the host enqueues a step in a few us
+    # One CUDA graph per layer holding the whole step (reshape_and_cache, then
+    # decode and its split-K combine, which start under their predecessor via
+    # programmatic dependent launch), and one holding only decode + combine
+    # for the kernel-level roofline timing.
     stream = torch.cuda.Stream(device)
-    g_rc, g_dec = [], []
+    g_step, g_dec = [], []
     with torch.cuda.stream(stream):
         for layer in range(POOL_LAYERS):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 reshape(layer)
-            g_rc.append(g)
+                decode(layer)
+            g_step.append(g)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 decode(layer)
             g_dec.append(g)
     torch.cuda.synchronize()
 
-    def step(s, evs=None):
-        layer = s % POOL_LAYERS
-        g_rc[layer].replay()
-        if evs is not None:
-            evs[0].record()
-        g_dec[layer].replay()
-        if evs is not None:
-            evs[1].record()
-
     for s in range(args.warmup):
-        step(s)
+        g_step[s % POOL_LAYERS].replay()
+        g_dec[s % POOL_LAYERS].replay()
     torch.cuda.synchronize()
 
     def barrier():
         if pg is not None:
             pg.barrier()
 
-    dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     gpu_ids = [int(x) for x in visible.split(",")][:max(world, 1)] if visible else list(range(max(world, 1)))
@@ -308,13 +302,24 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize()
     t_start.record()
     for s in range(args.steps):
-        step(s, dec_events[s])
+        g_step[s % POOL_LAYERS].replay()
     t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    step_ms = t_start.elapsed_time(t_end) / args.steps
+    # the decode kernel alone (decode + split-K combine), same K, same layer rotation
+    dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for s in range(args.steps):
+        dec_events[s][0].record()
+        g_dec[s % POOL_LAYERS].replay()
+        dec_events[s][1].record()
     torch.cuda.synchronize()
     barrier()
     if rank == 0:
         clocks.__exit__(None, None, None)
-    step_ms = t_start.elapsed_time(t_end) / args.steps
     dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec_events)
     if int(err.item()) != 0:
         raise RuntimeError(f"device error flag {int(err.item())}")
@@ -377,24 +382,28 @@ def run_b200(args, world, rank, local):
                        "sum_ctx_per_gpu": int(lens.sum()), "bytes_per_step_per_gpu": step_bytes,
                        "l2": "inputs larger than L2: 4-layer pool, consecutive steps use different layers "
                              "(~180 MB KV each)",
-                       "launch": "CUDA graph per kernel per layer", "parallelism": f"sequence-sharded x{world}"},
+                       "launch": "one CUDA graph per step (reshape_and_cache, decode, split-K combine; "
+                                 "programmatic dependent launch between them)",
+                       "parallelism": f"sequence-sharded x{world}"},
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
             "attn_layer_tok_per_s": round(BATCH * world / (step_ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "decode_fast_kernel<bf16>", "bytes_per_launch": decode_bytes(lens),
+                         "kernel": "decode_fast_kernel<bf16, 2> + decode_combine_kernel",
+                         "timing": "CUDA events around each decode+combine graph replay, K replays",
+                         "bytes_per_launch": decode_bytes(lens),
                          "avg_launch_ms": round(dec_ms, 5), "traffic": None},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
                     "path": "paged_decode_attention + write_tokens (reference-facing API), pinned host buffers"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    for g in g_rc + g_dec:
+    for g in g_step + g_dec:
         g.reset()
     if pg is not None:
         pg.destroy_process_group()

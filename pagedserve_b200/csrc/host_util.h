@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace psb {
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -28,6 +30,24 @@ int check_launch();
 inline void discard_stale_error() { (void)cudaGetLastError(); }
 
 CUtensorMapDataType dtype_to_tmap(int dtype);
+
+// Launch with programmatic stream serialization (the kernel may begin while
+// its stream predecessor is still running; see pdl_wait in common.cuh).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // 3-D tiled map over a paged pool viewed as [tiles, block_size, head_dim]
 // (one tile per (layer, block, kv head)), box = ``box_tiles`` whole

@@ -37,7 +37,7 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
-constexpr int kFastChunk = 256;        // tokens per split-K unit, fast path
+constexpr int kFastChunk = 128;        // tokens per split-K unit, fast path
 constexpr int kFastBlocksPerWarp = 4;  // 4 x 16 tokens
 constexpr int kTileBytes = 16 * 64 * 2;
 constexpr int kFastMaxGroup = 8;
@@ -478,6 +478,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   // HP contiguous 2 KB tiles lands at row r = chunk / 8, swizzled column
   // (chunk % 8) ^ (r % 8) - the 128-byte swizzle the ldmatrix offsets expect
   const uint32_t cp_col = lane & 7, cp_row0 = lane >> 3;
+  const uint32_t cp_dst_even = cp_row0 * 128 + ((cp_col ^ cp_row0) << 4);
+  const uint32_t cp_dst_odd = cp_row0 * 128 + ((cp_col ^ (cp_row0 + 4)) << 4);
 
   // Every warp's first unit is its global warp index; later units come from
   // the queue (numbered after those).  Grabs are issued one unit ahead and
@@ -525,15 +527,16 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     // that precedes every refill.
     if (ok) {
       const int64_t tile = zlayer + static_cast<int64_t>(blk) * p.hkv + iw.hg * HP;
-      const T* ksrc = kpool + tile * (16 * 64);
-      const T* vsrc = vpool + tile * (16 * 64);
-      // a 16 x 64 tile is 2 KB = 128 chunks: 4 per lane, HP tiles per box
+      const char* ksrc = reinterpret_cast<const char*>(kpool + tile * (16 * 64)) + lane * 16;
+      const char* vsrc = reinterpret_cast<const char*>(vpool + tile * (16 * 64)) + lane * 16;
+      // a 16 x 64 tile is 2 KB = 128 chunks: 4 per lane, HP tiles per box;
+      // chunk lane + 32 i sits at row 4 i + lane / 8, so the swizzled column
+      // alternates between two per-lane values
 #pragma unroll
       for (int i = 0; i < HP * 4; ++i) {
-        const uint32_t r = cp_row0 + 4 * i;  // 0 .. 16 * HP - 1
-        const uint32_t d = r * 128 + ((cp_col ^ (r & 7)) << 4);
-        cp_async16(sdst + d, ksrc + (lane + 32 * i) * 8);
-        cp_async16(sdst + Geo::kKV + d, vsrc + (lane + 32 * i) * 8);
+        const uint32_t d = sdst + i * 512 + ((i & 1) ? cp_dst_odd : cp_dst_even);
+        cp_async16(d, ksrc + i * 512);
+        cp_async16(d + Geo::kKV, vsrc + i * 512);
       }
     }
     if (first) {
@@ -575,6 +578,13 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     }
   };
 
+  // Everything above reads only lengths, tables and the workspace.  The pool
+  // and q may still be being written by the stream predecessor (a
+  // reshape_and_cache launched just before lets this kernel start early), so
+  // wait for it here; the combine kernel may launch as soon as every CTA is
+  // past this point.
+  pdl_wait();
+  pdl_launch_dependents();
   while (iu >= 0 && issued - consumed < static_cast<uint32_t>(kRing)) issue_one();
 
   // ---- consume side ------------------------------------------------------
@@ -770,6 +780,7 @@ constexpr int kCombThreads = 512;
 
 template <typename T, int HP>
 __global__ void __launch_bounds__(kCombThreads) decode_combine_kernel(const DecodeParams p) {
+  pdl_wait();  // every partial of the decode launch before is complete and visible
   const int groups = p.hkv / HP;
   const int i = blockIdx.x / groups, hg = blockIdx.x - (blockIdx.x / groups) * groups;
   const int32_t* order = p.plan;
@@ -1022,11 +1033,13 @@ int launch_fast(const DecodeParams& prm, cudaStream_t stream, int sms) {
   const int64_t grid =
       std::min<int64_t>(static_cast<int64_t>(sms) * occ, (prm.max_units + kFastWarps - 1) / kFastWarps);
   discard_stale_error();
-  decode_fast_kernel<T, HP><<<static_cast<unsigned>(grid), kFastThreads, smem, stream>>>(prm);
-  const int rc = check_launch();
-  if (rc != PSB_OK) return rc;
+  cudaError_t e = launch_pdl(decode_fast_kernel<T, HP>, dim3(static_cast<unsigned>(grid)), dim3(kFastThreads), smem,
+                             stream, prm);
+  if (e != cudaSuccess) return record_cuda_error(e);
   const int64_t merges = static_cast<int64_t>(prm.batch) * (prm.hkv / HP);
-  decode_combine_kernel<T, HP><<<static_cast<unsigned>(merges), kCombThreads, 0, stream>>>(prm);
+  e = launch_pdl(decode_combine_kernel<T, HP>, dim3(static_cast<unsigned>(merges)), dim3(kCombThreads), 0, stream,
+                 prm);
+  if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }
 

@@ -25,6 +25,9 @@ __global__ void __launch_bounds__(256) reshape_and_cache_kernel(
     int64_t vsh, char* __restrict__ k_cache, char* __restrict__ v_cache, const int64_t* __restrict__ slots,
     int32_t num_tokens, int64_t layer_base_tiles, int32_t hkv, int32_t block_size, int32_t row_bytes,
     int64_t pool_slots, int32_t* err) {
+  // a decode launched right after may start its prologue now (it waits for
+  // this grid before reading the pool)
+  pdl_launch_dependents();
   const int nvec = row_bytes / static_cast<int>(sizeof(V));
   const int64_t per_token = static_cast<int64_t>(hkv) * nvec;
   const int64_t total = per_token * num_tokens;
