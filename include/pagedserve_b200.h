@@ -119,6 +119,37 @@ int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, 
                      void* workspace, size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream);
 
 /*
+ * paged_decode_static: psb_paged_decode without a caller workspace.  It has
+ * no counterpart in the reference (whose Triton decode needs no scratch); it
+ * exists for callers that cannot allocate device memory where they launch
+ * decode (a pre-carved memory pool, an FFI host that owns no CUDA memory).
+ *
+ * The split-K scratch is a file-scope device array of
+ * psb_paged_decode_static_capacity() bytes (16 MiB) per device, reserved when
+ * its module loads; the call allocates nothing.  A geometry whose
+ * psb_paged_decode_workspace_size(...) exceeds that returns
+ * PSB_ERR_WORKSPACE (e.g. 64 sequences of up to 4096 tokens fit, 256 of up
+ * to 8192 do not).
+ *
+ * Set-up: the first call on each device looks up the array's address with
+ * that device current (and may load the module); make that first call before
+ * any stream capture.  Every call clears the scratch's counter region with an
+ * async memset on ``stream`` and then launches decode there.  The scratch is
+ * shared by every caller on a device: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller.
+ * Arguments, results and error behaviour are otherwise psb_paged_decode's.
+ */
+int psb_paged_decode_static(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
+                            int64_t o_stride_b, int64_t o_stride_h, const void* k_cache, const void* v_cache,
+                            const int32_t* block_tables, int64_t table_stride, const int32_t* context_lens,
+                            int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers, int64_t num_blocks,
+                            int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype,
+                            int32_t max_context, float scale, int32_t* error_flag, psb_stream_t stream);
+
+/* Bytes of the per-device scratch behind psb_paged_decode_static. */
+size_t psb_paged_decode_static_capacity(void);
+
+/*
  * varlen_prefill: packed ragged causal attention over freshly projected
  * q [total, q_heads, D], k/v [total, num_kv_heads, D] (element strides
  * (stride_t, stride_h), unit stride along D).  Sequence i owns rows

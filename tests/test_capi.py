@@ -91,3 +91,24 @@ def test_drop_in_rejects_cpu_query():
     cache.allocate("a", 1)
     with pytest.raises(ValueError, match="requires CUDA"):
         paged_decode_attention(torch.randn(1, 1, 1, 4), cache, ["a"], [0], 0)
+
+
+def test_static_decode_checks_need_no_gpu():
+    """The allocation-free decode rejects bad arguments and geometries whose
+    scratch would exceed its fixed capacity before any CUDA call."""
+    lib = _native.load()
+    cap = lib.psb_paged_decode_static_capacity()
+    assert cap == 16 << 20
+    null, fake = None, 256  # never dereferenced: every call below is rejected first
+    assert lib.psb_paged_decode_static(null, 0, 0, null, 0, 0, null, null, null, 0, null, 1, 14, 0, 1, 8, 2, 16, 64,
+                                       _native.PSB_BF16, 16, 0.125, null, null) == _native.PSB_ERR_INVALID
+    # 256 sequences of up to 8192 tokens need ~115 MiB of split-K scratch
+    assert lib.psb_paged_decode_workspace_size(256, 14, 2, 64, 16, 8192, _native.PSB_BF16) > cap
+    assert lib.psb_paged_decode_static(fake, 896, 64, fake, 896, 64, fake, fake, fake, 512, fake, 256, 14, 0, 1,
+                                       40000, 2, 16, 64, _native.PSB_BF16, 8192, 0.125, null,
+                                       null) == _native.PSB_ERR_WORKSPACE
+    # 64 sequences of up to 4096 tokens fit
+    assert 0 < lib.psb_paged_decode_workspace_size(64, 14, 2, 64, 16, 4096, _native.PSB_BF16) <= cap
+    # bad geometry (q heads not a multiple of kv heads)
+    assert lib.psb_paged_decode_static(fake, 0, 0, fake, 0, 0, fake, fake, fake, 8, fake, 4, 14, 0, 1, 8, 3, 16, 64,
+                                       _native.PSB_BF16, 128, 0.125, null, null) == _native.PSB_ERR_INVALID
