@@ -81,15 +81,19 @@ int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int64_t key_str
 
 /*
  * Workspace bytes psb_paged_decode needs for ``batch`` sequences whose
- * contexts are at most ``max_context`` tokens (split-K partials plus one
- * arrival counter per (sequence, kv head)).  The counter region must be zero
- * before the first call on a workspace (psb_paged_decode_workspace_init or a
- * memset); every call leaves it zero again.
+ * contexts are at most ``max_context`` tokens: split-K partials (fixed
+ * ~7.7 MB on the bf16/f16 path, which splits the pool blocks evenly over at
+ * most 160 CTAs) or, on the CUDA-core path, per-chunk partials plus one
+ * arrival counter per (sequence, kv head).  Returns the larger of the two,
+ * 0 for an invalid geometry.  The workspace needs no initialisation: each
+ * call clears what it relies on.
  */
 size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads, int32_t num_kv_heads, int32_t head_dim,
                                        int32_t block_size, int32_t max_context, int32_t dtype);
 
-/* Zero the counter region of a fresh workspace (async memset on ``stream``). */
+/* Zero the counter region of a workspace (async memset on ``stream``).  Kept
+ * for callers written against earlier versions; psb_paged_decode no longer
+ * needs it. */
 int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int32_t batch, int32_t num_kv_heads,
                                     psb_stream_t stream);
 
@@ -105,11 +109,16 @@ int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int
  * block_tables[b, :] (int32, row stride ``table_stride`` elements); q head h
  * reads kv head h / (q_heads / num_kv_heads).  query/out are [batch, q_heads,
  * head_dim] with element strides (stride_b, stride_h) and unit stride along
- * head_dim, in the pool's dtype.  Softmax and accumulation are fp32.  Long
- * contexts are split over CTAs (split-K) and merged in the same launch by
- * the last CTA to finish each (sequence, kv head).  ``max_context`` bounds
- * every context_lens[b] (host-known, e.g. table width x block_size).
- * Calls sharing one workspace must not overlap on the GPU.
+ * head_dim, in the pool's dtype.  Softmax and accumulation are fp32.
+ * ``max_context`` bounds every context_lens[b] (host-known, e.g. table width
+ * x block_size).  bf16/f16 with head_dim 64 and block_size 16 split the
+ * pool blocks of all sequences evenly over the SMs and merge the partials of
+ * sequences that span several warps in a second kernel on the same stream;
+ * other geometries run a CUDA-core kernel.  Context lengths and block tables
+ * are read before the kernel waits on its stream predecessor (programmatic
+ * dependent launch): they must not be written by the kernel launched
+ * immediately before this call.  Calls sharing one workspace must not overlap
+ * on the GPU.
  */
 int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out, int64_t o_stride_b,
                      int64_t o_stride_h, const void* k_cache, const void* v_cache, const int32_t* block_tables,

@@ -4,28 +4,22 @@
 // (pagedserve/attention/triton_paged_decode.py:10-95) with the numerics of its
 // PyTorch reference (pagedserve/attention/vectorized_batched_attention.py:79-159).
 //
-// Work decomposition.  A "unit" is (sequence b, kv head h, context chunk c).
-// Every CTA of a persistent grid first scans context_lens into a per-sequence
-// chunk prefix in shared memory, then walks units u = blockIdx.x, +gridDim.x, ...
-// Units are numbered u = (chunk_prefix[b] + c) * Hkv + h.  Sequences shorter
-// than one chunk finish in their single unit; longer ones write an fp32
-// partial (running max, sum, unnormalised output) to the workspace and the
-// last CTA to arrive for (b, h) - found with an atomic counter, no waiting -
-// merges the partials in the same launch.
-//
 // Fast path (bf16/f16, head_dim 64, block_size 16, up to 8 q heads per kv
-// head): 4 warps per CTA, each owns up to 4 pool blocks (64 tokens) of the
-// 256-token chunk.  Each warp's lane 0 pulls its K and V tiles (one
-// 16 x 64 tile per (layer, block, kv head), 2 KiB, contiguous in the pool)
-// into shared memory with TMA, 128-byte swizzled, completion on an mbarrier.
-// All q heads of the kv head sit in one m16n8k16 A fragment (rows = q heads),
-// so every K/V byte leaves HBM exactly once; QK^T and PV run on the tensor
-// pipe with fp32 accumulation, the softmax max/sum are quad shuffles.
-// Probabilities are rounded to the cache dtype before P.V, as the reference
-// does (vectorized_batched_attention.py:152-156).
+// head, or 16 with an odd kv-head count): the pool blocks of all sequences
+// are split evenly over the warps of a persistent grid (one CTA of 6 warps
+// per SM).  Each warp streams its blocks through a private shared-memory ring
+// with 16-byte cp.async copies, runs QK^T and PV on mma.sync m16n8k16 with
+// fp32 accumulation (all q heads of two kv heads packed into the 16 tile
+// rows, so every K/V byte leaves HBM once) and an online softmax reduced
+// with quad shuffles.  Probabilities are rounded to the cache dtype before
+// P.V, as the reference does (vectorized_batched_attention.py:152-156).  A
+// sequence that spans several warps leaves fp32 partials that
+// decode_combine_kernel, launched next on the same stream, merges.
 //
-// Generic path (fp32, or any other geometry): CUDA-core kernel with the same
-// unit decomposition and the same split-K finish, 64-token chunks.
+// Generic path (fp32, or any other geometry): CUDA-core kernel; a unit is
+// (sequence, kv head, 64-token chunk), and the last CTA to finish a split
+// sequence - an atomic ticket, no waiting - merges its partials in the same
+// launch.
 #include <algorithm>
 #include <type_traits>
 
@@ -38,9 +32,7 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kFastChunk = 128;        // tokens per split-K unit, fast path
-constexpr int kFastBlocksPerWarp = 4;  // 4 x 16 tokens
 constexpr int kTileBytes = 16 * 64 * 2;
-constexpr int kFastMaxGroup = 8;
 constexpr int kGenericChunk = 64;
 
 struct DecodeParams {
@@ -59,8 +51,9 @@ struct DecodeParams {
   float* part_o;     // [max_units, group, head_dim]
   float* part_ml;    // [max_units, group, 2]
   int32_t* counters; // [batch * hkv]
-  int32_t* work;     // [2]: next unit of the work queue, warps done
-  int32_t* plan;     // [2 * batch + 1]: longest-first order, chunk prefix (fast path)
+  int32_t* claims;   // [total_warps]: tail claims (fast path; zero between launches)
+  int32_t* plan;     // [batch + 1]: block prefix over sequences (fast path)
+  int32_t total_warps;  // warps of the fast-path decode grid
   int64_t max_units;
   int32_t* err;
 };
@@ -270,105 +263,73 @@ __device__ void finish_unit(const DecodeParams& p, const Unit& w, int64_t u, con
 }
 
 // ---------------------------------------------------------------------------
-// fast path: warp-pipelined TMA + mma.sync (bf16/f16, D = 64, block 16)
+// fast path: warp-streamed cp.async ring + mma.sync (bf16/f16, D = 64, block 16)
 // ---------------------------------------------------------------------------
 //
-// Each warp is an independent stream: it pulls units from a global work
-// queue (longest sequences first), keeps up to kRing pool blocks in flight
-// in its own shared-memory ring and consumes them one block at a time with
-// an online softmax.  No CTA-wide barrier follows the prologue; a finished
-// unit is written by the warp that finished it (directly, or as a split-K
-// partial merged by the last warp to finish its (sequence, head group)).
+// Work split.  The pool blocks every sequence's context occupies, taken in
+// (head group, sequence, block) order, form one list of N = Nb * groups
+// "items" (Nb = sum over sequences of max(1, ceil(ctx / 16))).  Warp w of
+// the grid's W warps owns items [a_w, e_w) = [w N / W, (w + 1) N / W).  It
+// streams the head [a_w, t_w) itself; the tail [t_w, e_w) (the last
+// 1 / kTailShare of the range) goes to a pool from which every warp whose
+// head is done takes tails through a global counter, so warps that stream
+// faster absorb the slower ones' work.  A part (head or tail) is a run of
+// "segments" (its share of one sequence): only its first and last segment
+// can belong to a sequence that another part also covers; those write an
+// fp32 partial (row max, row sum, unnormalised output) to a fixed slot -
+// 2 w + {0: first segment, 1: other} for the head of warp w, 2 W + 2 w +
+// {0, 1} for its tail - and decode_combine_kernel merges them.  Every other
+// segment writes its output.
+//
+// Each warp is an independent stream with its own shared-memory ring of
+// kRing slots (K and V of one block of HP packed kv heads, plus the q rows
+// with a segment's first block), filled by 16-byte cp.async copies, one
+// commit group per block.  No CTA-wide barrier follows the prologue.
 //
 // Row packing.  The 16 rows of the m16n8k16 tile hold the q heads of HP kv
 // heads: with HP = 2 rows 0-7 are the (<= 8) q heads of kv head 2p and rows
-// 8-15 those of kv head 2p+1, so one TMA box brings both heads' 16 x 64 tiles
-// (adjacent in the pool) and every accumulator register carries a real
+// 8-15 those of kv head 2p+1, so one block's copy brings both heads' 16 x 64
+// tiles (adjacent in the pool) and every accumulator register carries a real
 // output; with HP = 1 the 16 rows are up to 16 q heads of one kv head.  Each
-// K/V byte still leaves HBM exactly once.
+// K/V byte leaves HBM exactly once.
 constexpr int kFastWarps = 6;
 constexpr int kFastThreads = kFastWarps * 32;
-constexpr int kRing = 3;                           // slots per warp
-constexpr int kKeys = 64;                          // sort buckets: chunk counts >= 64 share the last
+constexpr int kRing = 3;              // slots per warp
+constexpr int kFastMinBlocks = 8;     // blocks per warp below which the grid shrinks
+constexpr int kTailShare = 4;         // 1 / kTailShare of every warp range goes to the pool
+constexpr int kGrabAhead = 4;         // line up the next part with this many blocks of a chunk left to issue
+constexpr int kStealTries = 3;        // claim attempts on the tails of the next 32 warps
+constexpr int kPartFloats = 16 * 64;  // one partial: 16 tile rows x 64 dims
+constexpr int kMaxFastBatch = 1 << 20;
 
 template <int HP>
 struct FastGeom {
-  static constexpr int kKV = HP * kTileBytes;      // K tiles of one block (HP heads)
-  static constexpr int kQ = 16 * 128;              // 16 q rows of 64 bf16/f16
-  static constexpr int kSlot = 2 * kKV + kQ;       // K box, V box, q rows
-  static constexpr int kRowsPerHead = 16 / HP;     // q heads per kv head the tile can hold
+  static constexpr int kKV = HP * kTileBytes;  // K tiles of one block (HP heads)
+  static constexpr int kQ = 16 * 128;          // 16 q rows of 64 bf16/f16
+  static constexpr int kSlot = 2 * kKV + kQ;   // K box, V box, q rows
   static size_t bytes(int batch) {
-    const size_t segs = (static_cast<size_t>(batch) + 31) / 32;
     return 1024 + static_cast<size_t>(kFastWarps) * kRing * kSlot +
-           sizeof(int32_t) * (3 * static_cast<size_t>(batch) + 1 + segs * kKeys) + 64;
+           sizeof(int32_t) * (2 * static_cast<size_t>(batch) + 1) + 64;
   }
 };
 
-__device__ __forceinline__ int chunks_of(int ctx, int chunk) { return ctx <= 0 ? 1 : (ctx + chunk - 1) / chunk; }
+__device__ __forceinline__ int blocks_of(int ctx) { return ctx <= 0 ? 1 : (ctx + 15) >> 4; }
 
-// s_ctx[b] = clamped context; order[i] = sequence at longest-first position i
-// (chunk count descending, ties by index); prefix[i] = exclusive prefix of
-// chunk counts along that order.  The order is a stable counting sort done by
-// the whole CTA: each warp ranks its 32 sequences among equal keys with
-// __match_any_sync, per-warp key histograms give each key's offset per warp.
-// Every CTA computes the same arrays, so unit numbers mean the same thing
-// everywhere; CTA 0 also leaves them in the workspace for the combine kernel.
-
-__device__ int build_lpt_prefix(const DecodeParams& p, int32_t* order, int32_t* prefix, int32_t* s_ctx,
-                                int32_t* whist) {
+// s_ctx[b] = clamped context; bpre[b] = exclusive prefix of blocks_of over
+// sequences, bpre[B] = Nb.  Every CTA computes the same arrays; CTA 0 also
+// leaves bpre in the workspace for the combine kernel.
+__device__ int build_block_prefix(const DecodeParams& p, int32_t* bpre, int32_t* s_ctx) {
   __shared__ int32_t warp_sums[kFastWarps];
-  __shared__ int32_t key_base[kKeys];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = p.batch;
-  const int nseg = (B + 31) / 32;  // 32-sequence segments, whist[seg][key]
-  for (int i = tid; i < nseg * kKeys; i += kFastThreads) whist[i] = 0;
-  for (int b = tid; b < B; b += kFastThreads) s_ctx[b] = clamp_ctx(p, b);
-  __syncthreads();
-  auto key_of = [&](int b) { return kKeys - min(chunks_of(s_ctx[b], kFastChunk), kKeys); };  // 0 = longest
-  // per-segment histograms
-  for (int seg = warp; seg < nseg; seg += kFastWarps) {
-    const int b = seg * 32 + lane;
-    const int key = b < B ? key_of(b) : kKeys;  // kKeys: padding, no bucket
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
-    if (key < kKeys && lane == __ffs(peers) - 1) whist[seg * kKeys + key] = __popc(peers);
-  }
-  __syncthreads();
-  // per key: exclusive prefix over segments (in place), total into key_base
-  for (int k = tid; k < kKeys; k += kFastThreads) {
-    int run = 0;
-    for (int seg = 0; seg < nseg; ++seg) {
-      const int c = whist[seg * kKeys + k];
-      whist[seg * kKeys + k] = run;
-      run += c;
-    }
-    key_base[k] = run;
-  }
-  __syncthreads();
-  if (warp == 0) {  // exclusive prefix over keys (ascending key = descending length)
-    int v0 = key_base[lane], v1 = key_base[lane + 32];
-    int incl0 = v0, incl1 = v1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int a0 = __shfl_up_sync(0xffffffffu, incl0, o), a1 = __shfl_up_sync(0xffffffffu, incl1, o);
-      if (lane >= o) incl0 += a0, incl1 += a1;
-    }
-    const int tot0 = __shfl_sync(0xffffffffu, incl0, 31);
-    key_base[lane] = incl0 - v0;
-    key_base[lane + 32] = tot0 + incl1 - v1;
-  }
-  __syncthreads();
-  for (int seg = warp; seg < nseg; seg += kFastWarps) {
-    const int b = seg * 32 + lane;
-    const int key = b < B ? key_of(b) : kKeys;
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
-    if (key < kKeys)
-      order[key_base[key] + whist[seg * kKeys + key] + __popc(peers & ((1u << lane) - 1u))] = b;
-  }
-  __syncthreads();
   const int per = (B + kFastThreads - 1) / kFastThreads;
   const int begin = min(tid * per, B), end = min(begin + per, B);
   int local = 0;
-  for (int i = begin; i < end; ++i) local += chunks_of(s_ctx[order[i]], kFastChunk);
+  for (int b = begin; b < end; ++b) {
+    const int n = clamp_ctx(p, b);
+    s_ctx[b] = n;
+    local += blocks_of(n);
+  }
   int incl = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -379,61 +340,45 @@ __device__ int build_lpt_prefix(const DecodeParams& p, int32_t* order, int32_t* 
   __syncthreads();
   int run = incl - local;
   for (int w = 0; w < warp; ++w) run += warp_sums[w];
-  for (int i = begin; i < end; ++i) {
-    prefix[i] = run;
-    run += chunks_of(s_ctx[order[i]], kFastChunk);
+  for (int b = begin; b < end; ++b) {
+    bpre[b] = run;
+    run += blocks_of(s_ctx[b]);
   }
   int total = 0;
   for (int w = 0; w < kFastWarps; ++w) total += warp_sums[w];
-  if (tid == 0) prefix[B] = total;
+  if (tid == 0) bpre[B] = total;
   __syncthreads();
-  if (blockIdx.x == 0) {
-    for (int i = tid; i < B; i += kFastThreads) p.plan[i] = order[i];
-    for (int i = tid; i <= B; i += kFastThreads) p.plan[B + i] = prefix[i];
-  }
+  if (blockIdx.x == 0)
+    for (int i = tid; i <= B; i += kFastThreads) p.plan[i] = bpre[i];
   return total;
 }
 
-// Unit u of the longest-first numbering: u = (prefix[i] + c) * groups + hg,
-// groups = hkv / HP head groups.
-struct FastUnit {
-  int b, hg, c, nch, ctx, nblk;
+// min(cap, left) for a 64-bit item count.
+__device__ __forceinline__ int clamp_items(int cap, int64_t left) {
+  return left < cap ? static_cast<int>(left) : cap;
+}
+
+// First item of warp w when n items are split over W warps: floor(n w / W).
+// n w < 2^53 is exact in double and the quotient is either an exact integer
+// or at least 1 / W away from one, so the floor is exact without a 64-bit
+// integer division.
+__device__ __forceinline__ int64_t warp_start(int64_t n_items, int64_t w, int64_t n_warps) {
+  return static_cast<int64_t>(floor(static_cast<double>(n_items * w) / static_cast<double>(n_warps)));
+}
+
+// Start of the tail of a warp range [a, e).
+__device__ __forceinline__ int64_t tail_start(int64_t a, int64_t e) { return e - (e - a) / kTailShare; }
+
+// A chunk: up to 32 consecutive items of one part, lane j holding item
+// beg + j - its raw block-table entry (-1 when the block holds no valid
+// token), flags (bits 1-5 valid tokens, 6 first of segment, 7 last of
+// segment), sequence | head group << 20 and partial slot (-1: the segment is
+// a whole sequence).
+struct Chunk {
+  int64_t beg;
+  int n;
+  int32_t blk, meta, seg, slot;
 };
-
-__device__ __forceinline__ FastUnit fast_unit(const DecodeParams& p, const int32_t* order, const int32_t* prefix,
-                                              const int32_t* s_ctx, int u, int groups) {
-  FastUnit w;
-  const int sc = u / groups;
-  w.hg = u - sc * groups;
-  const int i = find_seq(prefix, p.batch, sc);
-  w.b = order[i];
-  w.c = sc - prefix[i];
-  w.nch = prefix[i + 1] - prefix[i];
-  w.ctx = s_ctx[w.b];
-  w.nblk = max(1, (min(kFastChunk, w.ctx - w.c * kFastChunk) + 15) >> 4);
-  return w;
-}
-
-// Block ids of one unit: lane j < nblk holds entry j (-1 when out of range).
-__device__ __forceinline__ int32_t load_unit_table(const DecodeParams& p, const FastUnit& w, int lane) {
-  int32_t blk = -1;
-  const int ntok = min(kFastChunk, w.ctx - w.c * kFastChunk);
-  if (lane < w.nblk && lane * 16 < ntok) {
-    blk = __ldg(p.tables + w.b * p.table_stride + w.c * (kFastChunk / 16) + lane);
-    if (blk < 0 || blk >= p.num_blocks) {
-      flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
-      blk = -1;
-    }
-  }
-  return blk;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 
 // 16-byte asynchronous global -> shared copy (L2 only), grouped per block.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -448,21 +393,24 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   using Geo = FastGeom<HP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring_all = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  int32_t* order = reinterpret_cast<int32_t*>(ring_all + kFastWarps * kRing * Geo::kSlot);
-  int32_t* prefix = order + p.batch;
-  int32_t* s_ctx = prefix + p.batch + 1;
-  int32_t* whist = s_ctx + p.batch;  // [ceil(B / 32)][kKeys]
+  int32_t* bpre = reinterpret_cast<int32_t*>(ring_all + kFastWarps * kRing * Geo::kSlot);
+  int32_t* s_ctx = bpre + p.batch + 1;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int G = p.group;
+  const int B = p.batch;
   const int groups = p.hkv / HP;
   // tile rows this thread's accumulators cover: row g and row g + 8
   const bool row_lo = g < G;
   const bool row_hi = HP == 2 ? g < G : g + 8 < G;
   uint8_t* ring = ring_all + warp * kRing * Geo::kSlot;
-  const int total_units = build_lpt_prefix(p, order, prefix, s_ctx, whist) * groups;  // ends with __syncthreads
-  const int total_warps = gridDim.x * kFastWarps;
+  const int nb_total = build_block_prefix(p, bpre, s_ctx);  // ends with __syncthreads
+  const int64_t n_items = static_cast<int64_t>(nb_total) * groups;
+  const int n_warps = gridDim.x * kFastWarps;
+  const int gw = blockIdx.x * kFastWarps + warp;
+  const int64_t ibeg = warp_start(n_items, gw, n_warps);
+  const int64_t iend = tail_start(ibeg, warp_start(n_items, gw + 1, n_warps));  // the head
   const T* kpool = reinterpret_cast<const T*>(p.k_cache);
   const T* vpool = reinterpret_cast<const T*>(p.v_cache);
   const int64_t zlayer = static_cast<int64_t>(p.layer) * p.num_blocks * p.hkv;
@@ -481,52 +429,127 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   const uint32_t cp_dst_even = cp_row0 * 128 + ((cp_col ^ cp_row0) << 4);
   const uint32_t cp_dst_odd = cp_row0 * 128 + ((cp_col ^ (cp_row0 + 4)) << 4);
 
-  // Every warp's first unit is its global warp index; later units come from
-  // the queue (numbered after those).  Grabs are issued one unit ahead and
-  // their results read one unit later, so the atomic's round trip never
-  // stalls the warp.
-  auto grab_issue = [&]() -> int { return lane == 0 ? atomicAdd(p.work, 1) + total_warps : 0; };
-  auto grab_read = [&](int raw) -> int {
-    const int v = __shfl_sync(0xffffffffu, raw, 0);
-    return v < total_units ? v : -1;
+  // ---- parts and chunks --------------------------------------------------
+  // The current part is [pbeg, pend) with partial slots pbase + {0, 1}.  A
+  // warp streams its head, then its own tail if no other warp has claimed
+  // it, then tails it claims from the next 32 warps.  Claims are atomicCAS
+  // 0 -> owner (1) / thief (2) on one word per warp, which its owner clears
+  // when it starts.  (Every warp starts long before any warp looks at other
+  // tails; should an owner start that late and clear a claim already taken,
+  // the tail is streamed twice and both write the same bits to its slot.)
+  const int64_t my_a = warp_start(n_items, gw, n_warps), my_e = warp_start(n_items, gw + 1, n_warps);
+  const int64_t my_t = tail_start(my_a, my_e);
+  if (lane == 0) *reinterpret_cast<volatile int32_t*>(p.claims + gw) = 0;
+  int64_t pbeg = my_a, pend = my_t;
+  int32_t pbase = 2 * gw;
+  bool own_tail_tried = false, parts_left = true;
+  auto build_chunk = [&](int64_t cbeg) -> Chunk {
+    Chunk c;
+    c.beg = cbeg;
+    c.n = clamp_items(32, pend - cbeg);
+    c.blk = -1;
+    c.meta = 0;
+    c.seg = 0;
+    c.slot = -1;
+    if (lane < c.n) {
+      const int64_t i = cbeg + lane;
+      int hg = 0;
+      int64_t r = i;
+      while (r >= nb_total) {
+        r -= nb_total;
+        ++hg;
+      }
+      const int b = find_seq(bpre, B, static_cast<int>(r));
+      const int j = static_cast<int>(r) - bpre[b];
+      const int ctx = s_ctx[b], nblk = blocks_of(ctx);
+      const int valid = max(0, min(16, ctx - 16 * j));
+      const int64_t sf = i - j, sl = sf + nblk - 1;  // the sequence's first and last item
+      const bool first = i == pbeg || j == 0;
+      const bool last = i == pend - 1 || j == nblk - 1;
+      const bool partial = pbeg > sf || pend - 1 < sl;
+      c.slot = partial ? pbase + (sf > pbeg ? 1 : 0) : -1;
+      c.meta = (valid << 1) | (first ? 1 << 6 : 0) | (last ? 1 << 7 : 0);
+      c.seg = b | (hg << 20);
+      if (valid > 0) c.blk = __ldg(p.tables + static_cast<int64_t>(b) * p.table_stride + j);
+    }
+    return c;
   };
-
-  // ---- issue side --------------------------------------------------------
-  const int wid = blockIdx.x * kFastWarps + warp;
-  int iu = wid < total_units ? wid : -1;  // unit whose blocks are being issued
-  FastUnit iw{};
-  int32_t itab = -1;
-  int ib = 0;
-  if (iu >= 0) {
-    iw = fast_unit(p, order, prefix, s_ctx, iu, groups);
-    itab = load_unit_table(p, iw, lane);
+  // Make the next part current; false when this warp has nothing left.
+  auto next_part = [&]() -> bool {
+    if (!own_tail_tried) {
+      own_tail_tried = true;
+      if (my_e > my_t) {
+        int got = 0;
+        if (lane == 0) got = atomicCAS(p.claims + gw, 0, 1) == 0;
+        if (__shfl_sync(0xffffffffu, got, 0)) {
+          pbeg = my_t;
+          pend = my_e;
+          pbase = 2 * n_warps + 2 * gw;
+          return true;
+        }
+      }
+    }
+    for (int attempt = 0; attempt < kStealTries; ++attempt) {
+      const int v = gw + 1 + lane < n_warps ? gw + 1 + lane : gw + 1 + lane - n_warps;
+      int64_t va = 0, ve = 0, vt = 0;
+      bool open = false;
+      if (lane < n_warps - 1) {
+        va = warp_start(n_items, v, n_warps);
+        ve = warp_start(n_items, v + 1, n_warps);
+        vt = tail_start(va, ve);
+        open = ve > vt && *reinterpret_cast<volatile int32_t*>(p.claims + v) == 0;
+      }
+      const uint32_t cand = __ballot_sync(0xffffffffu, open);
+      if (!cand) return false;
+      const int pick = __ffs(cand) - 1;
+      int got = 0;
+      if (lane == pick) got = atomicCAS(p.claims + v, 0, 2) == 0;
+      if (__shfl_sync(0xffffffffu, got, pick)) {
+        pbeg = __shfl_sync(0xffffffffu, vt, pick);
+        pend = __shfl_sync(0xffffffffu, ve, pick);
+        pbase = 2 * n_warps + 2 * __shfl_sync(0xffffffffu, v, pick);
+        return true;
+      }
+    }
+    return false;
+  };
+  Chunk cur{}, nxt{};
+  bool c_ok = false, n_ok = false;
+  if (pend > pbeg) {  // the head's first two chunks, before the wait
+    cur = build_chunk(pbeg);
+    c_ok = true;
+    if (cur.beg + cur.n < pend) {
+      nxt = build_chunk(cur.beg + cur.n);
+      n_ok = true;
+    }
   }
-  int nu = iu >= 0 ? grab_read(grab_issue()) : -1;  // next unit: decoded, table prefetched
-  FastUnit nw{};
-  int32_t ntab = -1;
-  if (nu >= 0) {
-    nw = fast_unit(p, order, prefix, s_ctx, nu, groups);
-    ntab = load_unit_table(p, nw, lane);
-  }
-  int graw = nu >= 0 ? grab_issue() : 0;  // pending grab for the unit after nu
-  bool gpending = nu >= 0;
+  int ib = 0;  // next item of cur to issue
   uint32_t issued = 0, consumed = 0;
-  int32_t meta = 0;     // lane s: flags of ring slot s (bit 0 data, 1-5 valid tokens, 6 first, 7 last)
-  int32_t meta_u = -1;  // lane s: unit of ring slot s
+  int32_t meta = 0;       // lane s: flags of ring slot s (bit 0 data, 1-5 valid tokens, 6 first, 7 last)
+  int32_t meta_seg = 0;   // lane s: sequence | head group << 20 of ring slot s
+  int32_t meta_slot = 0;  // lane s: partial slot of ring slot s (-1: whole sequence)
 
-  // Copy one block (K and V of the HP packed heads, and the unit's q rows
+  // Copy one block (K and V of the HP packed heads, and the segment's q rows
   // with its first block) into the next ring slot as one cp.async group.
   auto issue_one = [&]() {
     const uint32_t slot = issued % kRing;
     const uint32_t sdst = smem_u32(ring + slot * Geo::kSlot);
-    const int32_t blk = __shfl_sync(0xffffffffu, itab, ib);
-    const int valid = max(0, min(16, iw.ctx - (iw.c * kFastChunk + ib * 16)));
-    const bool ok = blk >= 0 && valid > 0;
-    const bool first = ib == 0;
+    const int32_t blk = __shfl_sync(0xffffffffu, cur.blk, ib);
+    const int32_t mt = __shfl_sync(0xffffffffu, cur.meta, ib);
+    const int32_t sg = __shfl_sync(0xffffffffu, cur.seg, ib);
+    const int32_t sl = __shfl_sync(0xffffffffu, cur.slot, ib);
+    const int valid = (mt >> 1) & 31;
+    const bool first = (mt >> 6) & 1;
+    const int sb = sg & 0xfffff, shg = sg >> 20;
+    bool ok = valid > 0;
+    if (ok && (blk < 0 || blk >= p.num_blocks)) {
+      if (lane == 0) flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
+      ok = false;
+    }
     // The slot's previous contents were read (ldmatrix) before the __syncwarp
     // that precedes every refill.
     if (ok) {
-      const int64_t tile = zlayer + static_cast<int64_t>(blk) * p.hkv + iw.hg * HP;
+      const int64_t tile = zlayer + static_cast<int64_t>(blk) * p.hkv + shg * HP;
       const char* ksrc = reinterpret_cast<const char*>(kpool + tile * (16 * 64)) + lane * 16;
       const char* vsrc = reinterpret_cast<const char*>(vpool + tile * (16 * 64)) + lane * 16;
       // a 16 x 64 tile is 2 KB = 128 chunks: 4 per lane, HP tiles per box;
@@ -541,72 +564,86 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     }
     if (first) {
       // q rows of kv head hg*HP + s go to tile rows s*8 (HP = 2) or 0 (HP = 1)
-      const T* qb = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(iw.b) * p.qsb;
+      const T* qb = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(sb) * p.qsb;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = cp_row0 + 4 * i;  // tile row 0..15
         const int s = HP == 2 ? r >> 3 : 0;
         const int rr = HP == 2 ? r & 7 : r;
         if (rr < G) {
-          const T* src = qb + static_cast<int64_t>((iw.hg * HP + s) * G + rr) * p.qsh + cp_col * 8;
+          const T* src = qb + static_cast<int64_t>((shg * HP + s) * G + rr) * p.qsh + cp_col * 8;
           cp_async16(sdst + 2 * Geo::kKV + r * 128 + cp_col * 16, src);
         }
       }
     }
     cp_async_commit();
     if (lane == static_cast<int>(slot)) {
-      meta = (ok ? 1 : 0) | (valid << 1) | ((first ? 1 : 0) << 6) | ((ib == iw.nblk - 1 ? 1 : 0) << 7);
-      meta_u = iu;
+      meta = (ok ? 1 : 0) | (mt & ~1);
+      meta_seg = sg;
+      meta_slot = sl;
     }
     ++issued;
-    if (++ib == iw.nblk) {  // advance to the next unit
-      iu = nu;
-      iw = nw;
-      itab = ntab;
+    ++ib;
+    // cur is the last chunk of its part: line up the next part in time
+    if (!n_ok && parts_left && cur.n - ib <= kGrabAhead) {
+      parts_left = next_part();
+      if (parts_left) {
+        nxt = build_chunk(pbeg);
+        n_ok = true;
+      }
+    }
+    if (ib == cur.n) {  // advance to the next chunk
+      c_ok = n_ok;
+      cur = nxt;
       ib = 0;
-      nu = -1;
-      if (gpending) {
-        nu = grab_read(graw);
-        gpending = false;
-        if (nu >= 0) {
-          nw = fast_unit(p, order, prefix, s_ctx, nu, groups);
-          ntab = load_unit_table(p, nw, lane);
-          graw = grab_issue();
-          gpending = true;
-        }
+      n_ok = false;
+      if (c_ok && cur.beg + cur.n < pend) {  // the next chunk of the same part
+        nxt = build_chunk(cur.beg + cur.n);
+        n_ok = true;
       }
     }
   };
 
-  // Everything above reads only lengths, tables and the workspace.  The pool
-  // and q may still be being written by the stream predecessor (a
-  // reshape_and_cache launched just before lets this kernel start early), so
-  // wait for it here; the combine kernel may launch as soon as every CTA is
-  // past this point.
+  // Everything above reads only lengths and tables.  The pool and q may still
+  // be being written by the stream predecessor (a reshape_and_cache launched
+  // just before lets this kernel start early), so wait for it here; the
+  // combine kernel may launch as soon as every CTA is past this point.
   pdl_wait();
   pdl_launch_dependents();
-  while (iu >= 0 && issued - consumed < static_cast<uint32_t>(kRing)) issue_one();
+  if (!c_ok) {  // empty head: start on the tails
+    parts_left = next_part();
+    if (parts_left) {
+      cur = build_chunk(pbeg);
+      c_ok = true;
+      if (cur.beg + cur.n < pend) {
+        nxt = build_chunk(cur.beg + cur.n);
+        n_ok = true;
+      }
+    }
+  }
+  while (c_ok && issued - consumed < static_cast<uint32_t>(kRing)) issue_one();
 
   // ---- consume side ------------------------------------------------------
   uint32_t qa[4][4];   // A fragments per k-step (a0..a3)
   float o[8][4];       // rows g (c0, c1) and g + 8 (c2, c3), dims 8n + 2t + {0, 1}
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-  FastUnit cw{};
-  int cu = -1;
+  int32_t cseg = 0, cslot = -1;
   static_assert(kRing == 3, "the wait below assumes a three-slot ring");
   while (consumed != issued) {
     const uint32_t slot = consumed % kRing;
     const int32_t mt = __shfl_sync(0xffffffffu, meta, slot);
     const bool first = (mt >> 6) & 1, last = (mt >> 7) & 1;
     const int valid = (mt & 1) ? (mt >> 1) & 31 : 0;
-    if (first) cu = __shfl_sync(0xffffffffu, meta_u, slot);
+    if (first) {
+      cseg = __shfl_sync(0xffffffffu, meta_seg, slot);
+      cslot = __shfl_sync(0xffffffffu, meta_slot, slot);
+    }
     // the oldest copy group is complete once at most the newer ones are pending
     const uint32_t inflight = issued - consumed;
     if (inflight >= 3) cp_async_wait<2>(); else if (inflight == 2) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncwarp();  // every lane's copies are visible to every lane
     const uint32_t sbase = smem_u32(ring + slot * Geo::kSlot);
     if (first) {
-      cw = fast_unit(p, order, prefix, s_ctx, cu, groups);
       m_lo = m_hi = -INFINITY;
       l_lo = l_hi = 0.f;
 #pragma unroll
@@ -719,30 +756,32 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     }
     __syncwarp();
     ++consumed;
-    if (iu >= 0) issue_one();  // refill the slot just freed
+    if (c_ok) issue_one();  // refill the slot just freed
 
     if (last) {
-      // ---- finish the unit --------------------------------------------------
+      // ---- finish the segment ----------------------------------------------
       float ll = l_lo, lh = l_hi;
       ll += __shfl_xor_sync(0xffffffffu, ll, 1);
       lh += __shfl_xor_sync(0xffffffffu, lh, 1);
       ll += __shfl_xor_sync(0xffffffffu, ll, 2);
       lh += __shfl_xor_sync(0xffffffffu, lh, 2);
-      if (cw.nch == 1) {
-        const int qh_lo = HP == 2 ? (cw.hg * 2) * G + g : cw.hg * G + g;
-        const int qh_hi = HP == 2 ? (cw.hg * 2 + 1) * G + g : cw.hg * G + g + 8;
+      const int sb = cseg & 0xfffff, shg = (cseg >> 20) & 0xff;
+      if (cslot < 0) {
+        const int qh_lo = HP == 2 ? (shg * 2) * G + g : shg * G + g;
+        const int qh_hi = HP == 2 ? (shg * 2 + 1) * G + g : shg * G + g + 8;
         const float il = ll > 0.f ? 1.f / ll : 0.f, ih = lh > 0.f ? 1.f / lh : 0.f;
-        T* olo = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(cw.b) * p.osb + static_cast<int64_t>(qh_lo) * p.osh;
-        T* ohi = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(cw.b) * p.osb + static_cast<int64_t>(qh_hi) * p.osh;
+        T* olo = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(sb) * p.osb + static_cast<int64_t>(qh_lo) * p.osh;
+        T* ohi = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(sb) * p.osb + static_cast<int64_t>(qh_hi) * p.osh;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           if (row_lo) *reinterpret_cast<uint32_t*>(olo + n * 8 + 2 * t) = pack2<T>(o[n][0] * il, o[n][1] * il);
           if (row_hi) *reinterpret_cast<uint32_t*>(ohi + n * 8 + 2 * t) = pack2<T>(o[n][2] * ih, o[n][3] * ih);
         }
       } else {
-        // partial rows: 16 per unit, row g (lo) and g + 8 (hi)
-        float* po = p.part_o + static_cast<int64_t>(cu) * 16 * 64;
-        float* pml = p.part_ml + static_cast<int64_t>(cu) * 16 * 2;
+        // partial: 16 tile rows, row g (lo) and g + 8 (hi), merged after this
+        // launch by decode_combine_kernel
+        float* po = p.part_o + static_cast<int64_t>(cslot) * kPartFloats;
+        float* pml = p.part_ml + static_cast<int64_t>(cslot) * 32;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           *reinterpret_cast<float2*>(po + g * 64 + n * 8 + 2 * t) = make_float2(o[n][0], o[n][1]);
@@ -752,94 +791,146 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
           *reinterpret_cast<float2*>(pml + 2 * g) = make_float2(m_lo, ll);
           *reinterpret_cast<float2*>(pml + 2 * (g + 8)) = make_float2(m_hi, lh);
         }
-        // merged after this launch by decode_combine_kernel
       }
-    }
-  }
-  // The last warp of the launch leaves the work queue at zero for the next
-  // one.  The release-acquire "done" ticket orders every warp's grabs (a
-  // pending one included) before the reset.
-  if (lane == 0) {
-    if (atom_add_acq_rel_gpu(p.work + 1, 1) == total_warps - 1) {
-      p.work[0] = 0;
-      p.work[1] = 0;
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// split-K merge for the fast path: one CTA per (sequence, head group) with
-// more than one chunk, launched right after decode_fast_kernel on the same
-// stream (stream order makes every partial visible; no fences or atomics).
-// 16 warps: warp r first reduces row r's maximum over the chunks; then 4
-// groups of 128 threads take every 4th chunk, thread (row, 8-dim slice)
-// accumulating with full memory-level parallelism, and the groups are summed
-// through shared memory.
+// split-K merge for the fast path: one CTA per (sequence, head group).  The
+// CTA lists the parts that cover its sequence - the heads and tails of the
+// warp ranges it meets - from the block prefix the decode launch left in the
+// workspace; a sequence inside one part was finished there and the CTA
+// exits.  Otherwise thread (group, row, 8-dim slice) folds every
+// kCombGroups-th partial into a running (max, sum, output) with online
+// rescaling, kCombBatch partials' loads in flight at a time, and the groups
+// are merged through shared memory.
 // ---------------------------------------------------------------------------
-constexpr int kCombThreads = 512;
+constexpr int kCombGroups = 2;
+constexpr int kCombThreads = kCombGroups * 128;
+constexpr int kCombBatch = 4;
 
 template <typename T, int HP>
-__global__ void __launch_bounds__(kCombThreads) decode_combine_kernel(const DecodeParams p) {
-  pdl_wait();  // every partial of the decode launch before is complete and visible
+__global__ void __launch_bounds__(kCombThreads, 3) decode_combine_kernel(const DecodeParams p) {
+  pdl_wait();
   const int groups = p.hkv / HP;
-  const int i = blockIdx.x / groups, hg = blockIdx.x - (blockIdx.x / groups) * groups;
-  const int32_t* order = p.plan;
-  const int32_t* prefix = p.plan + p.batch;
-  const int nch = prefix[i + 1] - prefix[i];
-  if (nch <= 1) return;
-  const int b = order[i];
-  const int64_t u0 = static_cast<int64_t>(prefix[i]) * groups + hg;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float s_M[16];
-  __shared__ float s_acc[4][128][9];
-  __shared__ float s_l[4][16];
-  {
-    const int r = warp;  // 16 warps, one per tile row
-    float M = -INFINITY;
-    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(p.part_ml + (u0 + static_cast<int64_t>(c) * groups) * 32 + 2 * r));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (lane == 0) s_M[r] = M;
+  const int b = blockIdx.x / groups, hg = blockIdx.x - (blockIdx.x / groups) * groups;
+  const int32_t* bpre = p.plan;
+  const int64_t nb_total = bpre[p.batch];
+  const int64_t n_items = nb_total * groups;
+  const int64_t n_warps = p.total_warps;
+  const int64_t first = hg * nb_total + bpre[b], last = hg * nb_total + bpre[b + 1] - 1;
+  // warp ranges: the largest w with warp_start(w) <= item
+  auto warp_of = [&](int64_t item) {
+    int64_t w = static_cast<int64_t>(static_cast<double>(item) * static_cast<double>(n_warps) /
+                                     static_cast<double>(n_items));
+    w = min(max(w, int64_t(0)), n_warps - 1);
+    while (w + 1 < n_warps && warp_start(n_items, w + 1, n_warps) <= item) ++w;
+    while (w > 0 && warp_start(n_items, w, n_warps) > item) --w;
+    return w;
+  };
+  const int64_t wa = warp_of(first), wb = warp_of(last);
+  // part 2 i is the head of warp wa + i, part 2 i + 1 its tail; -1 when the
+  // part misses [first, last]
+  auto slot_of = [&](int64_t i) -> int64_t {
+    const int64_t w = wa + (i >> 1);
+    const int64_t a = warp_start(n_items, w, n_warps), e = warp_start(n_items, w + 1, n_warps);
+    const int64_t t = tail_start(a, e);
+    const int64_t lo = (i & 1) ? t : a, hi = (i & 1) ? e : t;
+    if (lo >= hi || hi <= first || lo > last) return -1;
+    return ((i & 1) ? 2 * n_warps + 2 * w : 2 * w) + (lo < first ? 1 : 0);
+  };
+  const int64_t n_parts = 2 * (wb - wa + 1);
+  if (wa == wb) {  // one warp range: a single part unless both its head and tail reach the sequence
+    const int64_t a = warp_start(n_items, wa, n_warps), e = warp_start(n_items, wa + 1, n_warps);
+    const int64_t t = tail_start(a, e);
+    if (t <= first || t > last || a == t) return;
   }
-  __syncthreads();
-  const int cg = tid >> 7, rq = tid & 127, r = rq >> 3, q8 = rq & 7;
-  const float M = s_M[r];
-  float acc[8];
+  const int tid = threadIdx.x, grp = tid >> 7, rq = tid & 127, r = rq >> 3, q8 = rq & 7;
+  float M = -INFINITY, L = 0.f, acc[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-  float l = 0.f;
-  if (M != -INFINITY) {
-#pragma unroll 4
-    for (int c = cg; c < nch; c += 4) {
-      const int64_t uc = u0 + static_cast<int64_t>(c) * groups;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + uc * 32 + 2 * r));
-      const float w = ml.x == -INFINITY ? 0.f : exp2f((ml.x - M) * p.scale_log2);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + uc * 16 * 64 + r * 64 + q8 * 8);
-      const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
-      l = fmaf(ml.y, w, l);
-      acc[0] = fmaf(v0.x, w, acc[0]); acc[1] = fmaf(v0.y, w, acc[1]);
-      acc[2] = fmaf(v0.z, w, acc[2]); acc[3] = fmaf(v0.w, w, acc[3]);
-      acc[4] = fmaf(v1.x, w, acc[4]); acc[5] = fmaf(v1.y, w, acc[5]);
-      acc[6] = fmaf(v1.z, w, acc[6]); acc[7] = fmaf(v1.w, w, acc[7]);
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  // slot ids of up to kCombThreads parts at a time, staged in shared memory
+  __shared__ int32_t s_slot[kCombThreads];
+  for (int64_t c0 = 0; c0 < n_parts; c0 += kCombThreads) {
+    const int nc = static_cast<int>(min(static_cast<int64_t>(kCombThreads), n_parts - c0));
+    __syncthreads();  // the previous chunk's slot ids are consumed
+    if (tid < nc) s_slot[tid] = static_cast<int32_t>(slot_of(c0 + tid));
+    __syncthreads();
+    for (int i0 = grp; i0 < nc; i0 += kCombGroups * kCombBatch) {
+      float2 ml[kCombBatch];
+      float4 va[kCombBatch], vb[kCombBatch];
+#pragma unroll
+      for (int k = 0; k < kCombBatch; ++k) {
+        const int i = i0 + kCombGroups * k;
+        ml[k] = make_float2(-INFINITY, 0.f);
+        va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int32_t slot_id = i < nc ? s_slot[i] : -1;
+        if (slot_id >= 0) {
+          ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + static_cast<int64_t>(slot_id) * 32 + 2 * r));
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + static_cast<int64_t>(slot_id) * kPartFloats +
+                                                              r * 64 + q8 * 8);
+          va[k] = __ldcg(src);
+          vb[k] = __ldcg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kCombBatch; ++k) {
+        if (ml[k].x == -INFINITY) continue;
+        if (ml[k].x > M) {
+          const float sc = exp2f((M - ml[k].x) * p.scale_log2);  // 0 while M is -inf
+          L *= sc;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] *= sc;
+          M = ml[k].x;
+        }
+        const float wt = exp2f((ml[k].x - M) * p.scale_log2);
+        L = fmaf(ml[k].y, wt, L);
+        acc[0] = fmaf(va[k].x, wt, acc[0]); acc[1] = fmaf(va[k].y, wt, acc[1]);
+        acc[2] = fmaf(va[k].z, wt, acc[2]); acc[3] = fmaf(va[k].w, wt, acc[3]);
+        acc[4] = fmaf(vb[k].x, wt, acc[4]); acc[5] = fmaf(vb[k].y, wt, acc[5]);
+        acc[6] = fmaf(vb[k].z, wt, acc[6]); acc[7] = fmaf(vb[k].w, wt, acc[7]);
+      }
     }
   }
+  constexpr int kOther = kCombGroups - 1;
+  __shared__ float s_acc[kOther][128][9];
+  __shared__ float s_ml[kOther][128][2];
+  if (grp > 0) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) s_acc[cg][rq][k] = acc[k];
-  if (q8 == 0) s_l[cg][r] = l;
+    for (int e = 0; e < 8; ++e) s_acc[grp - 1][rq][e] = acc[e];
+    s_ml[grp - 1][rq][0] = M;
+    s_ml[grp - 1][rq][1] = L;
+  }
   __syncthreads();
-  if (cg != 0) return;
-  const float L = s_l[0][r] + s_l[1][r] + s_l[2][r] + s_l[3][r];
-  const float inv = L > 0.f ? 1.f / L : 0.f;
+  if (grp > 0) return;
+  float Mx = M;
+#pragma unroll
+  for (int q = 0; q < kOther; ++q) Mx = fmaxf(Mx, s_ml[q][rq][0]);
+  float wq[kCombGroups];
+  wq[0] = M == -INFINITY ? 0.f : exp2f((M - Mx) * p.scale_log2);
+  float Lt = L * wq[0];
+#pragma unroll
+  for (int q = 0; q < kOther; ++q) {
+    const float mq = s_ml[q][rq][0];
+    wq[q + 1] = mq == -INFINITY ? 0.f : exp2f((mq - Mx) * p.scale_log2);
+    Lt = fmaf(s_ml[q][rq][1], wq[q + 1], Lt);
+  }
+  const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
   const int G = p.group;
   const int s = HP == 2 ? r >> 3 : 0, rr = HP == 2 ? r & 7 : r;
   if (rr >= G) return;
   const int qh = (hg * HP + s) * G + rr;
   T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.osb + static_cast<int64_t>(qh) * p.osh + q8 * 8;
 #pragma unroll
-  for (int k = 0; k < 8; k += 2) {
-    const float x = (s_acc[0][rq][k] + s_acc[1][rq][k] + s_acc[2][rq][k] + s_acc[3][rq][k]) * inv;
-    const float y = (s_acc[0][rq][k + 1] + s_acc[1][rq][k + 1] + s_acc[2][rq][k + 1] + s_acc[3][rq][k + 1]) * inv;
-    *reinterpret_cast<uint32_t*>(orow + k) = pack2<T>(x, y);
+  for (int e = 0; e < 8; e += 2) {
+    float x = acc[e] * wq[0], y = acc[e + 1] * wq[0];
+#pragma unroll
+    for (int q = 0; q < kOther; ++q) {
+      x = fmaf(s_acc[q][rq][e], wq[q + 1], x);
+      y = fmaf(s_acc[q][rq][e + 1], wq[q + 1], y);
+    }
+    *reinterpret_cast<uint32_t*>(orow + e) = pack2<T>(x * inv, y * inv);
   }
 }
 
@@ -985,53 +1076,79 @@ int fast_heads_per_unit(int dtype, int head_dim, int block_size, int group, int 
   return 0;
 }
 
-// Split-K geometry: units, rows per unit (the fast path always stores the
-// 16 packed tile rows) and the arrival-counter count.
+// Generic-path split-K geometry: units of (sequence, kv head, 64-token
+// chunk), ``group`` partial rows per unit, one arrival counter per
+// (sequence, kv head).
 struct SplitGeom {
   int chunk, rows, counters, batch;
   int64_t max_units;
 };
 
-SplitGeom split_geometry(int hp, int batch, int hkv, int group, int max_context) {
+SplitGeom split_geometry(int batch, int hkv, int group, int max_context) {
   SplitGeom sg;
-  sg.chunk = hp ? kFastChunk : kGenericChunk;
-  const int groups = hp ? hkv / hp : hkv;
+  sg.chunk = kGenericChunk;
   const int64_t per = std::max<int64_t>(1, (static_cast<int64_t>(max_context) + sg.chunk - 1) / sg.chunk);
-  sg.max_units = per * batch * groups;
-  sg.rows = hp ? 16 : group;
-  sg.counters = batch * groups;
+  sg.max_units = per * batch * hkv;
+  sg.rows = group;
+  sg.counters = batch * hkv;
   sg.batch = batch;
   return sg;
 }
 
 struct WorkspaceLayout {
-  size_t work_off, counters_off, plan_off, ml_off, o_off, total;
+  size_t counters_off, ml_off, o_off, total;
 };
 
-// [work queue: 2 x int32 | pad to 256][arrival counters: int32 per (sequence, head group)]
-// [plan: longest-first order and chunk prefix, 2 * batch + 1 int32]
-// [partial max/sum: max_units * rows * 2 f32][partial outputs: max_units * rows * head_dim f32]
-// Everything before ml_off must be zero before the first launch.
+// Generic path: [arrival counters: int32 per (sequence, kv head) | pad to 256]
+// [partial max/sum: max_units * rows * 2 f32][partial outputs: max_units * rows * head_dim f32].
+// Every call clears the counters first (the fast path keeps its block prefix
+// in the same bytes) and leaves them zero.
 WorkspaceLayout workspace_layout(const SplitGeom& sg, int head_dim) {
   WorkspaceLayout w;
-  w.work_off = 0;
-  w.counters_off = 256;
-  w.plan_off = align_up(w.counters_off + sizeof(int32_t) * static_cast<size_t>(sg.counters), 256);
-  w.ml_off = align_up(w.plan_off + sizeof(int32_t) * (2 * static_cast<size_t>(sg.batch) + 1), 256);
+  w.counters_off = 0;
+  w.ml_off = align_up(sizeof(int32_t) * static_cast<size_t>(sg.counters), 256);
   w.o_off = align_up(w.ml_off + sizeof(float) * static_cast<size_t>(sg.max_units) * sg.rows * 2, 256);
   w.total = w.o_off + sizeof(float) * static_cast<size_t>(sg.max_units) * sg.rows * head_dim;
   return w;
 }
 
+// Fast path: [tail claims: int32 per warp | pad to 256][block prefix: batch + 1 int32 | pad to 256]
+// [partial max/sum: slots * 16 * 2 f32][partial outputs: slots * 16 * 64 f32]:
+// two partial slots for the head and two for the tail of every warp range
+// of a grid of at most kMaxFastCtas CTAs (one per SM; B200 has 148).  The
+// decode kernel initialises the claims itself.
+constexpr int kMaxFastCtas = 160;
+
+struct FastLayout {
+  size_t claims_off, plan_off, ml_off, o_off, total;
+};
+
+FastLayout fast_layout(int batch) {
+  FastLayout f;
+  const size_t warps = static_cast<size_t>(kFastWarps) * kMaxFastCtas;
+  const size_t slots = 4 * warps;
+  f.claims_off = 0;
+  f.plan_off = align_up(sizeof(int32_t) * warps, 256);
+  f.ml_off = align_up(f.plan_off + sizeof(int32_t) * (static_cast<size_t>(batch) + 1), 256);
+  f.o_off = align_up(f.ml_off + sizeof(float) * slots * 32, 256);
+  f.total = f.o_off + sizeof(float) * slots * kPartFloats;
+  return f;
+}
+
 template <typename T, int HP>
-int launch_fast(const DecodeParams& prm, cudaStream_t stream, int sms) {
+int launch_fast(DecodeParams prm, cudaStream_t stream, int max_ctas) {
   const size_t smem = FastGeom<HP>::bytes(prm.batch);
   if (smem > 227 * 1024) return PSB_ERR_UNSUPPORTED;
   const void* kern = reinterpret_cast<const void*>(decode_fast_kernel<T, HP>);
   int occ = 0;
   if (!kernel_occupancy(kern, kFastThreads, smem, &occ) || occ < 1) return PSB_ERR_CUDA;
-  const int64_t grid =
-      std::min<int64_t>(static_cast<int64_t>(sms) * occ, (prm.max_units + kFastWarps - 1) / kFastWarps);
+  // an upper bound of the items from the host-known maximum context; small
+  // batches get fewer CTAs so each warp streams at least kFastMinBlocks blocks
+  const int64_t max_items = static_cast<int64_t>(prm.batch) * (prm.hkv / HP) *
+                            std::max<int64_t>(1, (static_cast<int64_t>(prm.max_context) + 15) / 16);
+  const int64_t want = (max_items + kFastWarps * kFastMinBlocks - 1) / (kFastWarps * kFastMinBlocks);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_ctas)));
+  prm.total_warps = grid * kFastWarps;
   discard_stale_error();
   cudaError_t e = launch_pdl(decode_fast_kernel<T, HP>, dim3(static_cast<unsigned>(grid)), dim3(kFastThreads), smem,
                              stream, prm);
@@ -1044,13 +1161,7 @@ int launch_fast(const DecodeParams& prm, cudaStream_t stream, int sms) {
 }
 
 template <typename T>
-int launch_decode(DecodeParams prm, int hp, cudaStream_t stream) {
-  const int sms = device_sm_count();
-  if (sms <= 0) return PSB_ERR_CUDA;
-  if constexpr (!std::is_same<T, float>::value) {
-    if (hp == 2) return launch_fast<T, 2>(prm, stream, sms);
-    if (hp == 1) return launch_fast<T, 1>(prm, stream, sms);
-  }
+int launch_generic(const DecodeParams& prm, cudaStream_t stream, int sms) {
   const size_t smem = generic_smem_bytes(prm.group, prm.head_dim, prm.batch);
   if (smem > 227 * 1024) return PSB_ERR_UNSUPPORTED;
   const void* kern = reinterpret_cast<const void*>(decode_generic_kernel<T>);
@@ -1067,7 +1178,7 @@ int launch_decode(DecodeParams prm, int hp, cudaStream_t stream) {
 int choose_path(int dtype, int head_dim, int block_size, int group, int hkv, int batch, const void* query,
                 int64_t qsb, int64_t qsh, const void* out, int64_t osb, int64_t osh, const void* kc, const void* vc) {
   const int hp = fast_heads_per_unit(dtype, head_dim, block_size, group, hkv);
-  if (!hp) return 0;
+  if (!hp || batch > kMaxFastBatch) return 0;
   const bool aligned = qsh % 8 == 0 && qsb % 8 == 0 && reinterpret_cast<uintptr_t>(query) % 16 == 0 &&
                        osh % 2 == 0 && osb % 2 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0 &&
                        reinterpret_cast<uintptr_t>(kc) % 16 == 0 && reinterpret_cast<uintptr_t>(vc) % 16 == 0;
@@ -1088,17 +1199,18 @@ extern "C" size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads
     return 0;
   const int group = q_heads / num_kv_heads;
   // sized for whichever path the geometry allows; large enough for the other
+  // (the fast path also depends on pointer alignment, known only at the call)
   const int hp = fast_heads_per_unit(dtype, head_dim, block_size, group, num_kv_heads);
-  const size_t fast = hp ? workspace_layout(split_geometry(hp, batch, num_kv_heads, group, max_context), head_dim).total : 0;
-  const size_t gen = workspace_layout(split_geometry(0, batch, num_kv_heads, group, max_context), head_dim).total;
+  const size_t fast = hp ? fast_layout(batch).total : 0;
+  const size_t gen = workspace_layout(split_geometry(batch, num_kv_heads, group, max_context), head_dim).total;
   return std::max(fast, gen);
 }
 
 extern "C" int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int32_t batch,
                                                int32_t num_kv_heads, psb_stream_t stream) {
+  if (workspace == nullptr || batch <= 0 || num_kv_heads <= 0) return PSB_ERR_INVALID;
   SplitGeom sg{kGenericChunk, 1, batch * num_kv_heads, batch, 0};
   const size_t need = workspace_layout(sg, 1).ml_off;
-  if (workspace == nullptr || batch <= 0 || num_kv_heads <= 0) return PSB_ERR_INVALID;
   if (workspace_bytes < need) return PSB_ERR_WORKSPACE;
   const cudaError_t e = cudaMemsetAsync(workspace, 0, need, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
@@ -1121,13 +1233,13 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
       max_context < 0 || table_stride < (max_context + block_size - 1) / block_size)
     return PSB_ERR_INVALID;
   if (dtype != PSB_F32 && dtype != PSB_F16 && dtype != PSB_BF16) return PSB_ERR_INVALID;
+  if (static_cast<int64_t>(num_layers) * num_blocks * num_kv_heads >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
   const int group = q_heads / num_kv_heads;
   const int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, query, q_stride_b, q_stride_h,
                              out, o_stride_b, o_stride_h, k_cache, v_cache);
-  const SplitGeom sg = split_geometry(hp, batch, num_kv_heads, group, max_context);
-  const WorkspaceLayout wl = workspace_layout(sg, head_dim);
-  if (workspace == nullptr || workspace_bytes < wl.total) return PSB_ERR_WORKSPACE;
-  if (static_cast<int64_t>(num_layers) * num_blocks * num_kv_heads >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
+  const int sms = device_sm_count();
+  if (sms <= 0) return PSB_ERR_CUDA;
+  if (workspace == nullptr) return PSB_ERR_WORKSPACE;
 
   DecodeParams p;
   p.q = static_cast<const char*>(query);
@@ -1150,21 +1262,42 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   p.block_size = block_size;
   p.head_dim = head_dim;
   p.max_context = max_context;
-  p.chunk = sg.chunk;
   p.num_blocks = num_blocks;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = error_flag;
+  p.total_warps = 0;
   char* ws = static_cast<char*>(workspace);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (hp) {
+    const FastLayout fl = fast_layout(batch);
+    const int max_ctas = std::min(sms, kMaxFastCtas);
+    if (workspace_bytes < fl.total) return PSB_ERR_WORKSPACE;
+    p.chunk = 0;
+    p.counters = nullptr;
+    p.claims = reinterpret_cast<int32_t*>(ws + fl.claims_off);
+    p.plan = reinterpret_cast<int32_t*>(ws + fl.plan_off);
+    p.part_ml = reinterpret_cast<float*>(ws + fl.ml_off);
+    p.part_o = reinterpret_cast<float*>(ws + fl.o_off);
+    p.max_units = 0;
+    if (dtype == PSB_BF16)
+      return hp == 2 ? launch_fast<__nv_bfloat16, 2>(p, s, max_ctas) : launch_fast<__nv_bfloat16, 1>(p, s, max_ctas);
+    return hp == 2 ? launch_fast<__half, 2>(p, s, max_ctas) : launch_fast<__half, 1>(p, s, max_ctas);
+  }
+  const SplitGeom sg = split_geometry(batch, num_kv_heads, group, max_context);
+  const WorkspaceLayout wl = workspace_layout(sg, head_dim);
+  if (workspace_bytes < wl.total) return PSB_ERR_WORKSPACE;
+  p.chunk = sg.chunk;
   p.counters = reinterpret_cast<int32_t*>(ws + wl.counters_off);
-  p.work = reinterpret_cast<int32_t*>(ws + wl.work_off);
-  p.plan = reinterpret_cast<int32_t*>(ws + wl.plan_off);
+  p.claims = nullptr;
+  p.plan = nullptr;
   p.part_ml = reinterpret_cast<float*>(ws + wl.ml_off);
   p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
   p.max_units = sg.max_units;
-  p.err = error_flag;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const cudaError_t ze = cudaMemsetAsync(p.counters, 0, sizeof(int32_t) * static_cast<size_t>(sg.counters), s);
+  if (ze != cudaSuccess) return record_cuda_error(ze);
   switch (dtype) {
-    case PSB_BF16: return launch_decode<__nv_bfloat16>(p, hp, s);
-    case PSB_F16: return launch_decode<__half>(p, hp, s);
-    default: return launch_decode<float>(p, 0, s);
+    case PSB_BF16: return launch_generic<__nv_bfloat16>(p, s, sms);
+    case PSB_F16: return launch_generic<__half>(p, s, sms);
+    default: return launch_generic<float>(p, s, sms);
   }
 }
