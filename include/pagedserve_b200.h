@@ -134,7 +134,7 @@ int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, 
  * decode (a pre-carved memory pool, an FFI host that owns no CUDA memory).
  *
  * The split-K scratch is a file-scope device array of
- * psb_paged_decode_static_capacity() bytes (16 MiB) per device, reserved when
+ * psb_paged_decode_static_capacity() bytes (32 MiB) per device, reserved when
  * its module loads; the call allocates nothing.  A geometry whose
  * psb_paged_decode_workspace_size(...) exceeds that returns
  * PSB_ERR_WORKSPACE (e.g. 64 sequences of up to 4096 tokens fit, 256 of up

@@ -51,7 +51,6 @@ struct DecodeParams {
   float* part_o;     // [max_units, group, head_dim]
   float* part_ml;    // [max_units, group, 2]
   int32_t* counters; // [batch * hkv]
-  int32_t* claims;   // [total_warps]: tail claims (fast path; zero between launches)
   int32_t* plan;     // [batch + 1]: block prefix over sequences (fast path)
   int32_t total_warps;  // warps of the fast-path decode grid
   int64_t max_units;
@@ -269,17 +268,16 @@ __device__ void finish_unit(const DecodeParams& p, const Unit& w, int64_t u, con
 // Work split.  The pool blocks every sequence's context occupies, taken in
 // (head group, sequence, block) order, form one list of N = Nb * groups
 // "items" (Nb = sum over sequences of max(1, ceil(ctx / 16))).  Warp w of
-// the grid's W warps owns items [a_w, e_w) = [w N / W, (w + 1) N / W).  It
-// streams the head [a_w, t_w) itself; the tail [t_w, e_w) (the last
-// 1 / kTailShare of the range) goes to a pool from which every warp whose
-// head is done takes tails through a global counter, so warps that stream
-// faster absorb the slower ones' work.  A part (head or tail) is a run of
-// "segments" (its share of one sequence): only its first and last segment
-// can belong to a sequence that another part also covers; those write an
-// fp32 partial (row max, row sum, unnormalised output) to a fixed slot -
-// 2 w + {0: first segment, 1: other} for the head of warp w, 2 W + 2 w +
-// {0, 1} for its tail - and decode_combine_kernel merges them.  Every other
-// segment writes its output.
+// the grid's W warps streams items [w N / W, (w + 1) N / W): every warp gets
+// the same number of blocks whatever the length distribution.  A warp's
+// range is a run of "segments" (its share of one sequence); a segment that
+// is a whole sequence writes its output, any other (only a range's first and
+// last can be) writes an fp32 partial (row max, row sum, unnormalised
+// output) to slot 2 w + {0: first segment, 1: last}, and
+// decode_combine_kernel merges the partials of every sequence that spans
+// several warps.  (Measured on the 256-sequence serving batch: per-warp
+// streaming rates differ by about 15 %, but handing out work dynamically -
+// atomic claims and steals - cost more per warp than the imbalance.)
 //
 // Each warp is an independent stream with its own shared-memory ring of
 // kRing slots (K and V of one block of HP packed kv heads, plus the q rows
@@ -296,9 +294,7 @@ constexpr int kFastWarps = 6;
 constexpr int kFastThreads = kFastWarps * 32;
 constexpr int kRing = 3;              // slots per warp
 constexpr int kFastMinBlocks = 8;     // blocks per warp below which the grid shrinks
-constexpr int kTailShare = 4;         // 1 / kTailShare of every warp range goes to the pool
-constexpr int kGrabAhead = 4;         // line up the next part with this many blocks of a chunk left to issue
-constexpr int kStealTries = 3;        // claim attempts on the tails of the next 32 warps
+
 constexpr int kPartFloats = 16 * 64;  // one partial: 16 tile rows x 64 dims
 constexpr int kMaxFastBatch = 1 << 20;
 
@@ -358,22 +354,28 @@ __device__ __forceinline__ int clamp_items(int cap, int64_t left) {
   return left < cap ? static_cast<int>(left) : cap;
 }
 
-// First item of warp w when n items are split over W warps: floor(n w / W).
-// n w < 2^53 is exact in double and the quotient is either an exact integer
-// or at least 1 / W away from one, so the floor is exact without a 64-bit
-// integer division.
-__device__ __forceinline__ int64_t warp_start(int64_t n_items, int64_t w, int64_t n_warps) {
-  return static_cast<int64_t>(floor(static_cast<double>(n_items * w) / static_cast<double>(n_warps)));
+// floor(x / d) for 0 <= x < 2^53 and d >= 1 given rd ~ 1 / d: a double
+// estimate corrected to the exact quotient with integer multiplies (no
+// division on the dependent path).
+__device__ __forceinline__ int64_t div_floor(int64_t x, int64_t d, double rd) {
+  int64_t q = static_cast<int64_t>(static_cast<double>(x) * rd);
+  if (q * d > x) --q;
+  if ((q + 1) * d <= x) ++q;
+  if (q * d > x) --q;
+  return q;
 }
 
-// Start of the tail of a warp range [a, e).
-__device__ __forceinline__ int64_t tail_start(int64_t a, int64_t e) { return e - (e - a) / kTailShare; }
+// First item of warp w when n items are split over W warps: floor(n w / W);
+// rw = 1 / W.
+__device__ __forceinline__ int64_t warp_start(int64_t n_items, int64_t w, int64_t n_warps, double rw) {
+  return div_floor(n_items * w, n_warps, rw);
+}
 
-// A chunk: up to 32 consecutive items of one part, lane j holding item
+// A chunk: up to 32 consecutive items of a warp's range, lane j holding item
 // beg + j - its raw block-table entry (-1 when the block holds no valid
-// token), flags (bits 1-5 valid tokens, 6 first of segment, 7 last of
-// segment), sequence | head group << 20 and partial slot (-1: the segment is
-// a whole sequence).
+// token), flags (bits 1-5 valid tokens, 6 first of its segment, 7 last of its
+// segment, 8 first block of its sequence, 9 last block of its sequence),
+// sequence | head group << 20 and partial slot.
 struct Chunk {
   int64_t beg;
   int n;
@@ -409,8 +411,6 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   const int64_t n_items = static_cast<int64_t>(nb_total) * groups;
   const int n_warps = gridDim.x * kFastWarps;
   const int gw = blockIdx.x * kFastWarps + warp;
-  const int64_t ibeg = warp_start(n_items, gw, n_warps);
-  const int64_t iend = tail_start(ibeg, warp_start(n_items, gw + 1, n_warps));  // the head
   const T* kpool = reinterpret_cast<const T*>(p.k_cache);
   const T* vpool = reinterpret_cast<const T*>(p.v_cache);
   const int64_t zlayer = static_cast<int64_t>(p.layer) * p.num_blocks * p.hkv;
@@ -429,28 +429,17 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   const uint32_t cp_dst_even = cp_row0 * 128 + ((cp_col ^ cp_row0) << 4);
   const uint32_t cp_dst_odd = cp_row0 * 128 + ((cp_col ^ (cp_row0 + 4)) << 4);
 
-  // ---- parts and chunks --------------------------------------------------
-  // The current part is [pbeg, pend) with partial slots pbase + {0, 1}.  A
-  // warp streams its head, then its own tail if no other warp has claimed
-  // it, then tails it claims from the next 32 warps.  Claims are atomicCAS
-  // 0 -> owner (1) / thief (2) on one word per warp, which its owner clears
-  // when it starts.  (Every warp starts long before any warp looks at other
-  // tails; should an owner start that late and clear a claim already taken,
-  // the tail is streamed twice and both write the same bits to its slot.)
-  const int64_t my_a = warp_start(n_items, gw, n_warps), my_e = warp_start(n_items, gw + 1, n_warps);
-  const int64_t my_t = tail_start(my_a, my_e);
-  if (lane == 0) *reinterpret_cast<volatile int32_t*>(p.claims + gw) = 0;
-  int64_t pbeg = my_a, pend = my_t;
-  int32_t pbase = 2 * gw;
-  bool own_tail_tried = false, parts_left = true;
+  // ---- chunks of this warp's range ----------------------------------------
+  const double rw = 1.0 / static_cast<double>(n_warps);
+  const int64_t my_a = warp_start(n_items, gw, n_warps, rw), my_e = warp_start(n_items, gw + 1, n_warps, rw);
   auto build_chunk = [&](int64_t cbeg) -> Chunk {
     Chunk c;
     c.beg = cbeg;
-    c.n = clamp_items(32, pend - cbeg);
+    c.n = clamp_items(32, my_e - cbeg);
     c.blk = -1;
     c.meta = 0;
     c.seg = 0;
-    c.slot = -1;
+    c.slot = 2 * gw;
     if (lane < c.n) {
       const int64_t i = cbeg + lane;
       int hg = 0;
@@ -463,71 +452,29 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       const int j = static_cast<int>(r) - bpre[b];
       const int ctx = s_ctx[b], nblk = blocks_of(ctx);
       const int valid = max(0, min(16, ctx - 16 * j));
-      const int64_t sf = i - j, sl = sf + nblk - 1;  // the sequence's first and last item
-      const bool first = i == pbeg || j == 0;
-      const bool last = i == pend - 1 || j == nblk - 1;
-      const bool partial = pbeg > sf || pend - 1 < sl;
-      c.slot = partial ? pbase + (sf > pbeg ? 1 : 0) : -1;
-      c.meta = (valid << 1) | (first ? 1 << 6 : 0) | (last ? 1 << 7 : 0);
+      c.slot = 2 * gw + (i - j > my_a ? 1 : 0);  // 0 for the range's first segment
+      c.meta = (valid << 1) | (j == 0 || i == my_a ? 1 << 6 : 0) | (j == nblk - 1 || i == my_e - 1 ? 1 << 7 : 0) |
+               (j == 0 ? 1 << 8 : 0) | (j == nblk - 1 ? 1 << 9 : 0);
       c.seg = b | (hg << 20);
       if (valid > 0) c.blk = __ldg(p.tables + static_cast<int64_t>(b) * p.table_stride + j);
     }
     return c;
   };
-  // Make the next part current; false when this warp has nothing left.
-  auto next_part = [&]() -> bool {
-    if (!own_tail_tried) {
-      own_tail_tried = true;
-      if (my_e > my_t) {
-        int got = 0;
-        if (lane == 0) got = atomicCAS(p.claims + gw, 0, 1) == 0;
-        if (__shfl_sync(0xffffffffu, got, 0)) {
-          pbeg = my_t;
-          pend = my_e;
-          pbase = 2 * n_warps + 2 * gw;
-          return true;
-        }
-      }
-    }
-    for (int attempt = 0; attempt < kStealTries; ++attempt) {
-      const int v = gw + 1 + lane < n_warps ? gw + 1 + lane : gw + 1 + lane - n_warps;
-      int64_t va = 0, ve = 0, vt = 0;
-      bool open = false;
-      if (lane < n_warps - 1) {
-        va = warp_start(n_items, v, n_warps);
-        ve = warp_start(n_items, v + 1, n_warps);
-        vt = tail_start(va, ve);
-        open = ve > vt && *reinterpret_cast<volatile int32_t*>(p.claims + v) == 0;
-      }
-      const uint32_t cand = __ballot_sync(0xffffffffu, open);
-      if (!cand) return false;
-      const int pick = __ffs(cand) - 1;
-      int got = 0;
-      if (lane == pick) got = atomicCAS(p.claims + v, 0, 2) == 0;
-      if (__shfl_sync(0xffffffffu, got, pick)) {
-        pbeg = __shfl_sync(0xffffffffu, vt, pick);
-        pend = __shfl_sync(0xffffffffu, ve, pick);
-        pbase = 2 * n_warps + 2 * __shfl_sync(0xffffffffu, v, pick);
-        return true;
-      }
-    }
-    return false;
-  };
   Chunk cur{}, nxt{};
   bool c_ok = false, n_ok = false;
-  if (pend > pbeg) {  // the head's first two chunks, before the wait
-    cur = build_chunk(pbeg);
+  if (my_e > my_a) {  // the range's first two chunks
+    cur = build_chunk(my_a);
     c_ok = true;
-    if (cur.beg + cur.n < pend) {
-      nxt = build_chunk(cur.beg + cur.n);
+    if (my_a + cur.n < my_e) {
+      nxt = build_chunk(my_a + cur.n);
       n_ok = true;
     }
   }
   int ib = 0;  // next item of cur to issue
   uint32_t issued = 0, consumed = 0;
-  int32_t meta = 0;       // lane s: flags of ring slot s (bit 0 data, 1-5 valid tokens, 6 first, 7 last)
+  int32_t meta = 0;       // lane s: ring slot s flags (bit 0 data, then as in Chunk::meta)
   int32_t meta_seg = 0;   // lane s: sequence | head group << 20 of ring slot s
-  int32_t meta_slot = 0;  // lane s: partial slot of ring slot s (-1: whole sequence)
+  int32_t meta_slot = 0;  // lane s: partial slot of ring slot s
 
   // Copy one block (K and V of the HP packed heads, and the segment's q rows
   // with its first block) into the next ring slot as one cp.async group.
@@ -583,21 +530,12 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       meta_slot = sl;
     }
     ++issued;
-    ++ib;
-    // cur is the last chunk of its part: line up the next part in time
-    if (!n_ok && parts_left && cur.n - ib <= kGrabAhead) {
-      parts_left = next_part();
-      if (parts_left) {
-        nxt = build_chunk(pbeg);
-        n_ok = true;
-      }
-    }
-    if (ib == cur.n) {  // advance to the next chunk
+    if (++ib == cur.n) {  // advance to the next chunk; build the one after it
       c_ok = n_ok;
       cur = nxt;
       ib = 0;
       n_ok = false;
-      if (c_ok && cur.beg + cur.n < pend) {  // the next chunk of the same part
+      if (c_ok && cur.beg + cur.n < my_e) {
         nxt = build_chunk(cur.beg + cur.n);
         n_ok = true;
       }
@@ -610,24 +548,14 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   // combine kernel may launch as soon as every CTA is past this point.
   pdl_wait();
   pdl_launch_dependents();
-  if (!c_ok) {  // empty head: start on the tails
-    parts_left = next_part();
-    if (parts_left) {
-      cur = build_chunk(pbeg);
-      c_ok = true;
-      if (cur.beg + cur.n < pend) {
-        nxt = build_chunk(cur.beg + cur.n);
-        n_ok = true;
-      }
-    }
-  }
   while (c_ok && issued - consumed < static_cast<uint32_t>(kRing)) issue_one();
 
   // ---- consume side ------------------------------------------------------
   uint32_t qa[4][4];   // A fragments per k-step (a0..a3)
   float o[8][4];       // rows g (c0, c1) and g + 8 (c2, c3), dims 8n + 2t + {0, 1}
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-  int32_t cseg = 0, cslot = -1;
+  int32_t cseg = 0, cslot = 0;
+  bool cfull = false;  // the current segment began at its sequence's first block
   static_assert(kRing == 3, "the wait below assumes a three-slot ring");
   while (consumed != issued) {
     const uint32_t slot = consumed % kRing;
@@ -637,6 +565,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     if (first) {
       cseg = __shfl_sync(0xffffffffu, meta_seg, slot);
       cslot = __shfl_sync(0xffffffffu, meta_slot, slot);
+      cfull = (mt >> 8) & 1;
     }
     // the oldest copy group is complete once at most the newer ones are pending
     const uint32_t inflight = issued - consumed;
@@ -766,7 +695,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       ll += __shfl_xor_sync(0xffffffffu, ll, 2);
       lh += __shfl_xor_sync(0xffffffffu, lh, 2);
       const int sb = cseg & 0xfffff, shg = (cseg >> 20) & 0xff;
-      if (cslot < 0) {
+      if (cfull && ((mt >> 9) & 1)) {  // the segment is the whole sequence
         const int qh_lo = HP == 2 ? (shg * 2) * G + g : shg * G + g;
         const int qh_hi = HP == 2 ? (shg * 2 + 1) * G + g : shg * G + g + 8;
         const float il = ll > 0.f ? 1.f / ll : 0.f, ih = lh > 0.f ? 1.f / lh : 0.f;
@@ -798,20 +727,19 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
 
 // ---------------------------------------------------------------------------
 // split-K merge for the fast path: one CTA per (sequence, head group).  The
-// CTA lists the parts that cover its sequence - the heads and tails of the
-// warp ranges it meets - from the block prefix the decode launch left in the
-// workspace; a sequence inside one part was finished there and the CTA
-// exits.  Otherwise thread (group, row, 8-dim slice) folds every
-// kCombGroups-th partial into a running (max, sum, output) with online
-// rescaling, kCombBatch partials' loads in flight at a time, and the groups
-// are merged through shared memory.
+// warps whose ranges meet the sequence follow from the block prefix the
+// decode launch left in the workspace; a sequence inside one warp's range
+// was finished there and the CTA exits.  Otherwise thread (row, 4-dim slice)
+// loads the partials of up to kCombBatch warps at once - one memory round
+// trip for most sequences - rescales them to their common maximum and writes
+// the normalised output.  Launched right after decode_fast_kernel on the same
+// stream; griddepcontrol.wait makes every partial visible.
 // ---------------------------------------------------------------------------
-constexpr int kCombGroups = 2;
-constexpr int kCombThreads = kCombGroups * 128;
-constexpr int kCombBatch = 4;
+constexpr int kCombThreads = 256;  // 16 tile rows x 16 slices of 4 dims
+constexpr int kCombBatch = 12;
 
 template <typename T, int HP>
-__global__ void __launch_bounds__(kCombThreads, 3) decode_combine_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kCombThreads, 2) decode_combine_kernel(const DecodeParams p) {
   pdl_wait();
   const int groups = p.hkv / HP;
   const int b = blockIdx.x / groups, hg = blockIdx.x - (blockIdx.x / groups) * groups;
@@ -820,118 +748,72 @@ __global__ void __launch_bounds__(kCombThreads, 3) decode_combine_kernel(const D
   const int64_t n_items = nb_total * groups;
   const int64_t n_warps = p.total_warps;
   const int64_t first = hg * nb_total + bpre[b], last = hg * nb_total + bpre[b + 1] - 1;
-  // warp ranges: the largest w with warp_start(w) <= item
-  auto warp_of = [&](int64_t item) {
-    int64_t w = static_cast<int64_t>(static_cast<double>(item) * static_cast<double>(n_warps) /
-                                     static_cast<double>(n_items));
-    w = min(max(w, int64_t(0)), n_warps - 1);
-    while (w + 1 < n_warps && warp_start(n_items, w + 1, n_warps) <= item) ++w;
-    while (w > 0 && warp_start(n_items, w, n_warps) > item) --w;
-    return w;
-  };
+  const double rw = 1.0 / static_cast<double>(n_warps), rn = 1.0 / static_cast<double>(n_items);
+  // the largest w with floor(n w / W) <= item, i.e. n w < (item + 1) W
+  auto warp_of = [&](int64_t item) { return min(n_warps - 1, div_floor((item + 1) * n_warps - 1, n_items, rn)); };
   const int64_t wa = warp_of(first), wb = warp_of(last);
-  // part 2 i is the head of warp wa + i, part 2 i + 1 its tail; -1 when the
-  // part misses [first, last]
-  auto slot_of = [&](int64_t i) -> int64_t {
-    const int64_t w = wa + (i >> 1);
-    const int64_t a = warp_start(n_items, w, n_warps), e = warp_start(n_items, w + 1, n_warps);
-    const int64_t t = tail_start(a, e);
-    const int64_t lo = (i & 1) ? t : a, hi = (i & 1) ? e : t;
-    if (lo >= hi || hi <= first || lo > last) return -1;
-    return ((i & 1) ? 2 * n_warps + 2 * w : 2 * w) + (lo < first ? 1 : 0);
-  };
-  const int64_t n_parts = 2 * (wb - wa + 1);
-  if (wa == wb) {  // one warp range: a single part unless both its head and tail reach the sequence
-    const int64_t a = warp_start(n_items, wa, n_warps), e = warp_start(n_items, wa + 1, n_warps);
-    const int64_t t = tail_start(a, e);
-    if (t <= first || t > last || a == t) return;
-  }
-  const int tid = threadIdx.x, grp = tid >> 7, rq = tid & 127, r = rq >> 3, q8 = rq & 7;
-  float M = -INFINITY, L = 0.f, acc[8];
+  if (wa == wb) return;  // inside one warp's range: written by the decode
+  const int tid = threadIdx.x, r = tid >> 4, q4 = tid & 15;
+  // item counts are below 2^31 and warps below 2^16: after one exact 64-bit
+  // division per batch, warp range starts step by n / W in 32-bit integers,
+  // plus one when the remainder wraps
+  const int nw32 = static_cast<int>(n_warps), first32 = static_cast<int>(first);
+  const int step = static_cast<int>(div_floor(n_items, n_warps, rw));
+  const int srem = static_cast<int>(n_items - static_cast<int64_t>(step) * n_warps);
+  const int w_last = static_cast<int>(wb);
+  float M = -INFINITY, L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w0 = static_cast<int>(wa); w0 <= w_last; w0 += kCombBatch) {
+    float2 ml[kCombBatch];
+    float4 v[kCombBatch];
+    const int64_t st64 = warp_start(n_items, w0, n_warps, rw);
+    int st = static_cast<int>(st64);
+    int rem = static_cast<int>(n_items * w0 - st64 * n_warps);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-  // slot ids of up to kCombThreads parts at a time, staged in shared memory
-  __shared__ int32_t s_slot[kCombThreads];
-  for (int64_t c0 = 0; c0 < n_parts; c0 += kCombThreads) {
-    const int nc = static_cast<int>(min(static_cast<int64_t>(kCombThreads), n_parts - c0));
-    __syncthreads();  // the previous chunk's slot ids are consumed
-    if (tid < nc) s_slot[tid] = static_cast<int32_t>(slot_of(c0 + tid));
-    __syncthreads();
-    for (int i0 = grp; i0 < nc; i0 += kCombGroups * kCombBatch) {
-      float2 ml[kCombBatch];
-      float4 va[kCombBatch], vb[kCombBatch];
-#pragma unroll
-      for (int k = 0; k < kCombBatch; ++k) {
-        const int i = i0 + kCombGroups * k;
-        ml[k] = make_float2(-INFINITY, 0.f);
-        va[k] = vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int32_t slot_id = i < nc ? s_slot[i] : -1;
-        if (slot_id >= 0) {
-          ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + static_cast<int64_t>(slot_id) * 32 + 2 * r));
-          const float4* src = reinterpret_cast<const float4*>(p.part_o + static_cast<int64_t>(slot_id) * kPartFloats +
-                                                              r * 64 + q8 * 8);
-          va[k] = __ldcg(src);
-          vb[k] = __ldcg(src + 1);
-        }
+    for (int k = 0; k < kCombBatch; ++k) {
+      ml[k] = make_float2(-INFINITY, 0.f);
+      v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      int nx = st + step;
+      rem += srem;
+      if (rem >= nw32) {
+        rem -= nw32;
+        ++nx;
       }
-#pragma unroll
-      for (int k = 0; k < kCombBatch; ++k) {
-        if (ml[k].x == -INFINITY) continue;
-        if (ml[k].x > M) {
-          const float sc = exp2f((M - ml[k].x) * p.scale_log2);  // 0 while M is -inf
-          L *= sc;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] *= sc;
-          M = ml[k].x;
-        }
-        const float wt = exp2f((ml[k].x - M) * p.scale_log2);
-        L = fmaf(ml[k].y, wt, L);
-        acc[0] = fmaf(va[k].x, wt, acc[0]); acc[1] = fmaf(va[k].y, wt, acc[1]);
-        acc[2] = fmaf(va[k].z, wt, acc[2]); acc[3] = fmaf(va[k].w, wt, acc[3]);
-        acc[4] = fmaf(vb[k].x, wt, acc[4]); acc[5] = fmaf(vb[k].y, wt, acc[5]);
-        acc[6] = fmaf(vb[k].z, wt, acc[6]); acc[7] = fmaf(vb[k].w, wt, acc[7]);
+      const int s0 = st;
+      st = nx;
+      if (w0 + k <= w_last && s0 != nx) {  // an empty range wrote nothing
+        const int slot_id = 2 * (w0 + k) + (s0 < first32 ? 1 : 0);
+        ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + slot_id * 16 + r);
+        v[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o) + slot_id * (kPartFloats / 4) + r * 16 + q4);
       }
     }
-  }
-  constexpr int kOther = kCombGroups - 1;
-  __shared__ float s_acc[kOther][128][9];
-  __shared__ float s_ml[kOther][128][2];
-  if (grp > 0) {
+    float mb = M;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s_acc[grp - 1][rq][e] = acc[e];
-    s_ml[grp - 1][rq][0] = M;
-    s_ml[grp - 1][rq][1] = L;
-  }
-  __syncthreads();
-  if (grp > 0) return;
-  float Mx = M;
+    for (int k = 0; k < kCombBatch; ++k) mb = fmaxf(mb, ml[k].x);
+    if (mb == -INFINITY) continue;
+    const float sc = exp2f((M - mb) * p.scale_log2);  // 0 while M is -inf
+    M = mb;
+    L *= sc;
 #pragma unroll
-  for (int q = 0; q < kOther; ++q) Mx = fmaxf(Mx, s_ml[q][rq][0]);
-  float wq[kCombGroups];
-  wq[0] = M == -INFINITY ? 0.f : exp2f((M - Mx) * p.scale_log2);
-  float Lt = L * wq[0];
+    for (int e = 0; e < 4; ++e) acc[e] *= sc;
 #pragma unroll
-  for (int q = 0; q < kOther; ++q) {
-    const float mq = s_ml[q][rq][0];
-    wq[q + 1] = mq == -INFINITY ? 0.f : exp2f((mq - Mx) * p.scale_log2);
-    Lt = fmaf(s_ml[q][rq][1], wq[q + 1], Lt);
+    for (int k = 0; k < kCombBatch; ++k) {
+      if (ml[k].x == -INFINITY) continue;
+      const float wt = exp2f((ml[k].x - M) * p.scale_log2);
+      L = fmaf(ml[k].y, wt, L);
+      acc[0] = fmaf(v[k].x, wt, acc[0]);
+      acc[1] = fmaf(v[k].y, wt, acc[1]);
+      acc[2] = fmaf(v[k].z, wt, acc[2]);
+      acc[3] = fmaf(v[k].w, wt, acc[3]);
+    }
   }
-  const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
   const int G = p.group;
   const int s = HP == 2 ? r >> 3 : 0, rr = HP == 2 ? r & 7 : r;
   if (rr >= G) return;
+  const float inv = L > 0.f ? 1.f / L : 0.f;
   const int qh = (hg * HP + s) * G + rr;
-  T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.osb + static_cast<int64_t>(qh) * p.osh + q8 * 8;
-#pragma unroll
-  for (int e = 0; e < 8; e += 2) {
-    float x = acc[e] * wq[0], y = acc[e + 1] * wq[0];
-#pragma unroll
-    for (int q = 0; q < kOther; ++q) {
-      x = fmaf(s_acc[q][rq][e], wq[q + 1], x);
-      y = fmaf(s_acc[q][rq][e + 1], wq[q + 1], y);
-    }
-    *reinterpret_cast<uint32_t*>(orow + e) = pack2<T>(x * inv, y * inv);
-  }
+  T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.osb + static_cast<int64_t>(qh) * p.osh + q4 * 4;
+  *reinterpret_cast<uint32_t*>(orow) = pack2<T>(acc[0] * inv, acc[1] * inv);
+  *reinterpret_cast<uint32_t*>(orow + 2) = pack2<T>(acc[2] * inv, acc[3] * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -1101,8 +983,8 @@ struct WorkspaceLayout {
 
 // Generic path: [arrival counters: int32 per (sequence, kv head) | pad to 256]
 // [partial max/sum: max_units * rows * 2 f32][partial outputs: max_units * rows * head_dim f32].
-// Every call clears the counters first (the fast path keeps its block prefix
-// in the same bytes) and leaves them zero.
+// Every call clears the counters first (the fast path keeps scratch in the
+// same bytes) and leaves them zero.
 WorkspaceLayout workspace_layout(const SplitGeom& sg, int head_dim) {
   WorkspaceLayout w;
   w.counters_off = 0;
@@ -1112,24 +994,21 @@ WorkspaceLayout workspace_layout(const SplitGeom& sg, int head_dim) {
   return w;
 }
 
-// Fast path: [tail claims: int32 per warp | pad to 256][block prefix: batch + 1 int32 | pad to 256]
-// [partial max/sum: slots * 16 * 2 f32][partial outputs: slots * 16 * 64 f32]:
-// two partial slots for the head and two for the tail of every warp range
-// of a grid of at most kMaxFastCtas CTAs (one per SM; B200 has 148).  The
-// decode kernel initialises the claims itself.
+// Fast path: [block prefix: batch + 1 int32 | pad to 256][partial max/sum:
+// slots * 16 * 2 f32][partial outputs: slots * 16 * 64 f32], two partial
+// slots per warp of a grid of at most kMaxFastCtas CTAs (one per SM; B200 has
+// 148).  Nothing needs initialising.
 constexpr int kMaxFastCtas = 160;
 
 struct FastLayout {
-  size_t claims_off, plan_off, ml_off, o_off, total;
+  size_t plan_off, ml_off, o_off, total;
 };
 
 FastLayout fast_layout(int batch) {
   FastLayout f;
-  const size_t warps = static_cast<size_t>(kFastWarps) * kMaxFastCtas;
-  const size_t slots = 4 * warps;
-  f.claims_off = 0;
-  f.plan_off = align_up(sizeof(int32_t) * warps, 256);
-  f.ml_off = align_up(f.plan_off + sizeof(int32_t) * (static_cast<size_t>(batch) + 1), 256);
+  const size_t slots = 2 * static_cast<size_t>(kFastWarps) * kMaxFastCtas;
+  f.plan_off = 0;
+  f.ml_off = align_up(sizeof(int32_t) * (static_cast<size_t>(batch) + 1), 256);
   f.o_off = align_up(f.ml_off + sizeof(float) * slots * 32, 256);
   f.total = f.o_off + sizeof(float) * slots * kPartFloats;
   return f;
@@ -1175,15 +1054,20 @@ int launch_generic(const DecodeParams& prm, cudaStream_t stream, int sms) {
 
 // Which path a call takes (the fast path bulk-copies 16-byte q rows and
 // writes the output in 4-byte pairs).
-int choose_path(int dtype, int head_dim, int block_size, int group, int hkv, int batch, const void* query,
-                int64_t qsb, int64_t qsh, const void* out, int64_t osb, int64_t osh, const void* kc, const void* vc) {
+int choose_path(int dtype, int head_dim, int block_size, int group, int hkv, int batch, int max_context,
+                const void* query, int64_t qsb, int64_t qsh, const void* out, int64_t osb, int64_t osh, const void* kc,
+                const void* vc) {
   const int hp = fast_heads_per_unit(dtype, head_dim, block_size, group, hkv);
   if (!hp || batch > kMaxFastBatch) return 0;
   const bool aligned = qsh % 8 == 0 && qsb % 8 == 0 && reinterpret_cast<uintptr_t>(query) % 16 == 0 &&
                        osh % 2 == 0 && osb % 2 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0 &&
                        reinterpret_cast<uintptr_t>(kc) % 16 == 0 && reinterpret_cast<uintptr_t>(vc) % 16 == 0;
   const size_t smem = hp == 2 ? FastGeom<2>::bytes(batch) : FastGeom<1>::bytes(batch);
-  return aligned && smem <= 227 * 1024 ? hp : 0;
+  // item indices are int32 inside the kernel
+  const int64_t max_items = static_cast<int64_t>(batch) * (hkv / hp) *
+                            std::max<int64_t>(1, (static_cast<int64_t>(max_context) + 15) / 16);
+  const bool fits = max_items < (int64_t(1) << 31);
+  return aligned && fits && smem <= 227 * 1024 ? hp : 0;
 }
 
 }  // namespace
@@ -1235,8 +1119,8 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   if (dtype != PSB_F32 && dtype != PSB_F16 && dtype != PSB_BF16) return PSB_ERR_INVALID;
   if (static_cast<int64_t>(num_layers) * num_blocks * num_kv_heads >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
   const int group = q_heads / num_kv_heads;
-  const int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, query, q_stride_b, q_stride_h,
-                             out, o_stride_b, o_stride_h, k_cache, v_cache);
+  const int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, max_context, query, q_stride_b,
+                             q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache);
   const int sms = device_sm_count();
   if (sms <= 0) return PSB_ERR_CUDA;
   if (workspace == nullptr) return PSB_ERR_WORKSPACE;
@@ -1274,7 +1158,6 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
     if (workspace_bytes < fl.total) return PSB_ERR_WORKSPACE;
     p.chunk = 0;
     p.counters = nullptr;
-    p.claims = reinterpret_cast<int32_t*>(ws + fl.claims_off);
     p.plan = reinterpret_cast<int32_t*>(ws + fl.plan_off);
     p.part_ml = reinterpret_cast<float*>(ws + fl.ml_off);
     p.part_o = reinterpret_cast<float*>(ws + fl.o_off);
@@ -1288,7 +1171,6 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   if (workspace_bytes < wl.total) return PSB_ERR_WORKSPACE;
   p.chunk = sg.chunk;
   p.counters = reinterpret_cast<int32_t*>(ws + wl.counters_off);
-  p.claims = nullptr;
   p.plan = nullptr;
   p.part_ml = reinterpret_cast<float*>(ws + wl.ml_off);
   p.part_o = reinterpret_cast<float*>(ws + wl.o_off);

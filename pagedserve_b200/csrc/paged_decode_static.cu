@@ -20,10 +20,10 @@
 
 namespace {
 
-constexpr size_t kStaticScratchBytes = size_t(16) << 20;
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
 constexpr int kMaxDevices = 64;
 
-// Split-K partials, work queue and arrival counters for one call at a time
+// Split-K partials, steal state and arrival counters for one call at a time
 // per device.  Zero-initialised at module load; the counter prefix is cleared
 // again before every call.
 __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];

@@ -98,7 +98,7 @@ def test_static_decode_checks_need_no_gpu():
     scratch would exceed its fixed capacity before any CUDA call."""
     lib = _native.load()
     cap = lib.psb_paged_decode_static_capacity()
-    assert cap == 16 << 20
+    assert cap == 32 << 20
     null, fake = None, 256  # never dereferenced: every call below is rejected first
     assert lib.psb_paged_decode_static(null, 0, 0, null, 0, 0, null, null, null, 0, null, 1, 14, 0, 1, 8, 2, 16, 64,
                                        _native.PSB_BF16, 16, 0.125, null, null) == _native.PSB_ERR_INVALID
