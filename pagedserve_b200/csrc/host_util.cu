@@ -139,6 +139,26 @@ bool encode_matrix_map(CUtensorMap* map, const void* base, int64_t rows, int64_t
   return true;
 }
 
+bool encode_rows_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int head_dim, int64_t row_stride,
+                     int64_t head_stride, int box_rows, CUtensorMapDataType dt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const size_t esz = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_stride * esz), static_cast<cuuint64_t>(row_stride * esz)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), 1u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = 10000 + static_cast<int>(r);
+    return false;
+  }
+  return true;
+}
+
 }  // namespace psb
 
 extern "C" const char* psb_version(void) { return "pagedserve_b200 0.1.0 sm_100a"; }

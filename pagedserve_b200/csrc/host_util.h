@@ -55,6 +55,13 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int block_size, int head_dim,
                           int box_tiles, CUtensorMapDataType dt);
 
+// 3-D tiled map over [rows, heads, head_dim] rows of a packed token batch
+// (element strides row_stride, head_stride; unit stride along head_dim):
+// box = box_rows rows of one head, 128-byte swizzle.  head_dim * element
+// size must be 128 bytes, both strides multiples of 16 bytes.
+bool encode_rows_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int head_dim, int64_t row_stride,
+                     int64_t head_stride, int box_rows, CUtensorMapDataType dt);
+
 // 2-D tiled map over a row-major [rows, cols] matrix with row pitch
 // ``row_stride_elems``; box = box_rows x box_cols, 128-byte swizzle.
 bool encode_matrix_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,

@@ -94,3 +94,44 @@ def test_malformed_cu_seqlens_reported():
     ops.varlen_prefill(q, k, v, cu, 15, error_flag=err)
     torch.cuda.synchronize()
     assert int(err.item()) & 32
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_varlen_strided_fused_qkv(dtype):
+    """q, k and v as column slices of one fused QKV projection [T, (Hq + 2 Hkv) * D]
+    (row stride 1152 elements), the layout the model's projection produces."""
+    from pagedserve_b200 import ops
+    lens = [200, 1, 130, 64]
+    c = varlen_case(11, lens, dtype=dtype)
+    t, hq, hkv, d = c["q"].shape[0], 14, 2, 64
+    qkv = torch.zeros(t, (hq + 2 * hkv) * d, dtype=to_dev(c["q"], dtype).dtype, device="cuda")
+    qkv[:, :hq * d] = to_dev(c["q"], dtype).reshape(t, hq * d)
+    qkv[:, hq * d:(hq + hkv) * d] = to_dev(c["k"], dtype).reshape(t, hkv * d)
+    qkv[:, (hq + hkv) * d:] = to_dev(c["v"], dtype).reshape(t, hkv * d)
+    q = qkv[:, :hq * d].view(t, hq, d)
+    k = qkv[:, hq * d:(hq + hkv) * d].view(t, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].view(t, hkv, d)
+    assert q.stride(0) == (hq + 2 * hkv) * d
+    cu = torch.from_numpy(np.asarray(c["cu_seqlens"], dtype=np.int32)).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ops.varlen_prefill(q, k, v, cu, max(lens), error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    exact = ora.varlen_causal_attention(c["q"], c["k"], c["v"], c["cu_seqlens"])
+    mx, mean = err_stats(out, exact)
+    max_tol, mean_tol = TOL[dtype]
+    assert mx <= max_tol and mean <= mean_tol, (mx, mean)
+
+
+def test_varlen_longest_prompt():
+    """A 2048-token prompt (16 query blocks, the heaviest tile streams 16 key
+    tiles) packed with short ones; checked on its first, middle and last rows."""
+    lens = [3, 2048, 129]
+    c = varlen_case(5, lens)
+    out = _run(c)
+    a, b = int(c["cu_seqlens"][1]), int(c["cu_seqlens"][2])
+    exact = ora.varlen_causal_attention(c["q"], c["k"], c["v"], c["cu_seqlens"])
+    mx, mean = err_stats(out, exact)
+    assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
+    mx, _ = err_stats(out[b - 128:b], exact[b - 128:b])
+    assert mx <= 2e-2
