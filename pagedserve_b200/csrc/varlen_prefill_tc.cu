@@ -6,28 +6,38 @@
 // q [T, Hq, 64], k/v [T, Hkv, 64], sequence i = rows cu[i] .. cu[i+1], causal
 // within each sequence, q head h reads kv head h / (Hq / Hkv).
 //
-// One CTA (five warps, 80 KB of shared memory, 256 TMEM columns, two CTAs
-// per SM) takes a tile of 128 query rows of one q head.  Tiles are numbered
-// heaviest first (a tile of query block i needs 2 (i + 1) key tiles), with
-// the q heads of a tile adjacent so they share K/V through L2.  Warp 4 is the
-// producer: one lane issues every TMA copy and every tcgen05.mma.  Warps 0-3
-// (thread r = TMEM lane r = query row r) do the softmax.  They meet only on
-// mbarriers, so the tensor core works while the softmax runs.  Per key tile
-// j of 64 keys, streamed through a 4-stage TMA ring (128-byte swizzle):
-//   producer: S_{j+1} = Q K_{j+1}^T (four tcgen05.mma, M 128, N 64, K 16;
-//   fp32 into one of two TMEM buffers) as soon as K_{j+1} lands;
-//   softmax: thread r loads its row of S_j, masks keys past its own position
-//   or past the sequence and stores P = exp2(S - m) rounded to the input type
+// Work: a tile is 128 query rows of one q head; a tile of query block i
+// streams 2 (i + 1) key tiles of 64 keys.  Tiles are numbered heaviest first
+// (a stable counting sort of the sequences by query blocks, built by every
+// CTA in shared memory), the q heads of a tile adjacent so they share K/V
+// through L2.  A persistent grid of two CTAs per SM takes them in snake order.
+//
+// A CTA is six warps, 96 KB of shared memory and 256 TMEM columns.  Warps 0-3
+// (thread r = TMEM lane r = query row r of the tile) do the softmax; one lane
+// of warp 4 issues the Q loads and S = Q K^T, one lane of warp 5 the K/V
+// loads and O += P V.  They meet only on mbarriers, so the tensor core works
+// while the softmax runs.  A global step counter across the CTA's tiles
+// drives the 4-stage K/V ring (128-byte swizzle, requested three steps ahead,
+// into the next tile too), the two TMEM S buffers and the barrier phases; Q
+// is double-buffered per tile.  Per key tile (step):
+//   producer: S = Q K^T (four tcgen05.mma, M 128, N 64, K 16; fp32 into one of
+//   two TMEM S buffers) one step ahead of the softmax;
+//   softmax: thread r loads its row of S, masks keys past its own position or
+//   past the sequence and stores P = exp2(S - m) rounded to the input type
 //   (as the reference rounds the probabilities before P.V,
-//   paged_attention.py:291-302) to its TMEM lane, two keys per column.  m is a lazily updated row max: only when a row's max grows by
-//   more than 2^8 is the O accumulated so far in TMEM rescaled (so P stays
-//   below 256 and most steps touch no O at all);
-//   producer: O += P_j V_j (four tcgen05.mma with P read from TMEM, N 64, V as
-//   an MN-major operand, accumulating in TMEM across tiles), then requests K/V
-//   tile j + 3 into the stage P.V_{j-1} freed.
-// Every mbarrier wait is bounded; on a timeout the CTA records
-// PSB_DEVERR_TIMEOUT, waits (bounded) for its copies in flight, frees TMEM and
-// returns.
+//   paged_attention.py:291-302) to its TMEM lane, two keys per column.  m is
+//   a lazily updated row max: only when a row's max grows by more than 2^8 is
+//   the O accumulated so far in TMEM rescaled (so P stays below 256 and most
+//   steps touch no O at all);
+//   producer: O += P V (four tcgen05.mma with P read from TMEM, N 64, V as an
+//   MN-major operand; the first step of a tile overwrites O, which the
+//   softmax warps have read for the previous tile before they got there).
+// Every mbarrier wait is bounded and each phase is waited for before the
+// barrier can move two phases on; on a timeout a CTA records
+// PSB_DEVERR_TIMEOUT, lets its copies and MMAs in flight land (bounded), frees
+// TMEM and returns.
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "varlen_prefill.h"
@@ -36,21 +46,23 @@ namespace psb {
 namespace {
 
 constexpr int kSoftmaxThreads = 128;  // warps 0-3: warp w <-> TMEM lanes and tile rows 32 w .. 32 w + 31
-constexpr int kTcThreads = kSoftmaxThreads + 32;  // warp 4: TMA and MMA issue
+constexpr int kTcThreads = kSoftmaxThreads + 64;  // warp 4: Q loads and Q K^T; warp 5: K/V loads and P V
 constexpr int kBM = 128;         // query rows per tile
-constexpr int kBN = 64;          // keys per tile
+constexpr int kBN = 64;          // keys per step
 constexpr int kDim = 64;
-constexpr uint32_t kTile = kBM * kDim * 2;   // bytes of the Q tile and of P (16 KB)
+constexpr uint32_t kTile = kBM * kDim * 2;    // bytes of one Q tile (16 KB)
 constexpr uint32_t kKvTile = kBN * kDim * 2;  // bytes of one K or V tile (8 KB)
-constexpr int kKvStages = 4;                 // K/V ring depth
+constexpr int kKvStages = 4;                  // K/V ring depth
+constexpr int kKvAhead = kKvStages;           // K/V of step g + kKvAhead is requested once P.V of step g is done
 constexpr uint32_t kTmemCols = 256;  // S buffers: cols [0, 64), [64, 128); O: [128, 192); P: [192, 224)
-constexpr uint32_t kPCol = 192;
+constexpr uint32_t kSCol = 0, kOCol = 128, kPCol = 192;
 constexpr float kRescaleLog2 = 8.f;  // rescale O when a row max grows by more than 2^8
-constexpr uint32_t kSCol = 0, kOCol = 128;
-// dynamic shared memory (1024-byte aligned): Q | K ring | V ring
-constexpr uint32_t kOffQ = 0, kOffK = kTile, kOffV = kTile + kKvStages * kKvTile;
-constexpr uint32_t kSmemTiles = kTile + 2 * kKvStages * kKvTile;
-constexpr int kMaxLevels = 1024;  // query blocks per sequence (128 K tokens)
+// dynamic shared memory (1024-byte aligned): Q0 | Q1 | K ring | V ring | barriers | tile tables
+constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 2 * kTile + kKvStages * kKvTile;
+constexpr uint32_t kSmemTiles = 2 * kTile + 2 * kKvStages * kKvTile;
+constexpr uint32_t kSmemBars = 128;
+constexpr int kMaxLevels = 1024;    // query blocks per sequence (128 K tokens)
+constexpr int kMaxTcSeqs = 2048;    // sequences whose order fits the shared tile table
 
 // Length of sequence s; 0 unless 0 <= cu[s] <= cu[s+1] <= total (a malformed
 // batch is reported by the caller's check and must not be read out of bounds).
@@ -60,88 +72,113 @@ __device__ __forceinline__ int seq_len(const PrefillParams& p, int s) {
   return min(b - a, p.max_seqlen);
 }
 
+struct TileInfo {
+  int q0, len, qblk, head, kvh, n_kv;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 2)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kSmemTiles);
-  uint64_t* bar_kv = bar_q + 1;  // [kKvStages]
-  uint64_t* bar_s = bar_q + 5;   // [2]
-  uint64_t* bar_o = bar_q + 7;
-  uint64_t* bar_p = bar_q + 8;   // softmax step done: P written, S and the O tile read
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_q + 9);
-  int32_t* s_info = reinterpret_cast<int32_t*>(bar_q + 10);   // seq, level
-  int32_t* s_count = reinterpret_cast<int32_t*>(bar_q + 11);  // [max_level + 1] sequences per top level
+  uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kSmemTiles);  // [2]
+  uint64_t* bar_kv = bar_q + 2;                                      // [kKvStages]
+  uint64_t* bar_s = bar_q + 2 + kKvStages;                           // [2]
+  uint64_t* bar_sfree = bar_s + 2;  // [2] S buffer read by the softmax
+  uint64_t* bar_o = bar_sfree + 2;
+  uint64_t* bar_p = bar_o + 1;      // softmax step done: P written
+  uint64_t* bar_qfree = bar_p + 1;  // a tile's Q K^T done
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_qfree + 1);
+  const int max_level = (p.max_seqlen + kBM - 1) / kBM;
+  int32_t* s_lstart = reinterpret_cast<int32_t*>(smem + kSmemTiles + kSmemBars);  // [max_level + 1]
+  int32_t* s_cnt = s_lstart + (max_level + 1);   // [max_level + 1] sequences with more than i blocks
+  int32_t* s_fill = s_cnt + (max_level + 1);     // [max_level + 1] placement cursors
+  int32_t* s_sorted = s_fill + (max_level + 1);  // [num_seqs] sequences by query blocks, descending, stable
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hq = p.hq, group = p.hq / p.hkv;
-  const int head = static_cast<int>(blockIdx.x % hq);
-  const int tile = static_cast<int>(blockIdx.x / hq);
   // cu_seqlens, q, k and v may come from the stream predecessor
   pdl_wait();
 
-  // ---- tile -> (sequence, query block), heaviest blocks first ------------
-  const int max_level = (p.max_seqlen + kBM - 1) / kBM;
-  for (int i = tid; i <= max_level; i += kTcThreads) s_count[i] = 0;
+  // ---- tile table: sequences sorted by query blocks (stable), level starts
+  for (int i = tid; i <= max_level; i += kTcThreads) s_cnt[i] = 0;
   __syncthreads();
   for (int s = tid; s < p.num_seqs; s += kTcThreads) {
     const int nb = (seq_len(p, s) + kBM - 1) / kBM;
-    if (nb > 0) atomicAdd(&s_count[nb - 1], 1);  // sequences whose top level is nb - 1
+    if (nb > 0) atomicAdd(&s_cnt[nb - 1], 1);  // histogram of top levels
   }
   __syncthreads();
-  if (warp == 0) {
-    // tiles at level i = sequences with more than i blocks = suffix sum of s_count
-    int level = -1, rank = 0, run = 0, above = 0;
-    for (int i = max_level - 1; i >= 0 && level < 0; --i) {
-      above += s_count[i];  // sequences reaching level i
-      if (tile < run + above) {
-        level = i;
-        rank = tile - run;
-      }
-      run += above;
+  if (tid == 0) {
+    // c_i = sequences with more than i blocks (suffix sums); level i holds
+    // tiles [lstart_i, lstart_i + c_i), levels numbered from the top
+    int run = 0, start = 0;
+    for (int i = max_level - 1; i >= 0; --i) {
+      run += s_cnt[i];
+      s_cnt[i] = run;
+      s_lstart[i] = start;
+      start += run;
     }
-    int seq = -1;
-    if (level >= 0) {  // the rank-th sequence (by index) with more than ``level`` blocks
-      int seen = 0;
-      for (int s0 = 0; s0 < p.num_seqs && seq < 0; s0 += 32) {
-        const int s = s0 + lane;
-        bool hit = false;
-        if (s < p.num_seqs) hit = (seq_len(p, s) + kBM - 1) / kBM > level;
-        const uint32_t m = __ballot_sync(0xffffffffu, hit);
-        const int c = __popc(m);
-        if (rank < seen + c) {
-          uint32_t mm = m;
-          for (int k = 0; k < rank - seen; ++k) mm &= mm - 1;
-          seq = s0 + __ffs(mm) - 1;
-        }
-        seen += c;
+    s_cnt[max_level] = 0;
+    s_lstart[max_level] = start;  // tiles in all
+    for (int i = 0; i <= max_level; ++i) s_fill[i] = i < max_level ? s_cnt[i + 1] : 0;  // first slot of key i + 1
+  }
+  __syncthreads();
+  if (warp == 0) {  // stable placement: sequences with nb blocks go after those with more
+    for (int s0 = 0; s0 < p.num_seqs; s0 += 32) {
+      const int s = s0 + lane;
+      const int nb = s < p.num_seqs ? (seq_len(p, s) + kBM - 1) / kBM : 0;
+      const uint32_t peers = __match_any_sync(0xffffffffu, nb);
+      if (nb > 0) {
+        const int pos = s_fill[nb - 1] + __popc(peers & ((1u << lane) - 1u));
+        s_sorted[pos] = s;
       }
-    }
-    if (lane == 0) {
-      s_info[0] = seq;
-      s_info[1] = level;
+      __syncwarp();
+      if (nb > 0 && lane == __ffs(peers) - 1) s_fill[nb - 1] += __popc(peers);
+      __syncwarp();
     }
   }
   __syncthreads();
-  const int seq = s_info[0], qblk = s_info[1];
-  if (seq < 0) return;  // grid is sized for an upper bound of the tiles
-
-  const int q0 = p.cu[seq];
-  const int len = seq_len(p, seq);
-  const int kvh = head / group;
-  const int n_kv = min(2 * (qblk + 1), (len + kBN - 1) / kBN);
+  // tiles are dealt to the CTAs in snake order (round r left to right when
+  // even, right to left when odd), which evens out the heaviest-first list
+  const int total_tiles = s_lstart[max_level] * hq;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int rounds = total_tiles / G, rem = total_tiles - rounds * G;
+  const int my_tiles = rounds + (((rounds & 1) ? G - 1 - c : c) < rem ? 1 : 0);
+  if (my_tiles == 0) return;
+  // k-th tile of this CTA
+  auto tile_of = [&](int k) -> TileInfo {
+    const int t = k * G + ((k & 1) ? G - 1 - c : c);
+    const int tt = t / hq;
+    int lo = 0, hi = max_level - 1;  // the smallest level i with lstart_i <= T
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (s_lstart[mid] <= tt) hi = mid; else lo = mid + 1;
+    }
+    TileInfo ti;
+    const int seq = s_sorted[tt - s_lstart[lo]];
+    ti.qblk = lo;
+    ti.head = t - tt * hq;
+    ti.kvh = ti.head / group;
+    ti.q0 = p.cu[seq];
+    ti.len = seq_len(p, seq);
+    ti.n_kv = min(2 * (lo + 1), (ti.len + kBN - 1) / kBN);
+    return ti;
+  };
   const uint32_t s_base = smem_u32(smem);
 
-  // ---- set-up: barriers, TMEM ----------------------------------------------
+  // ---- set-up: barriers, TMEM ------------------------------------------------
   if (tid == 0) {
     mbar_init(bar_q, 1);
+    mbar_init(bar_q + 1, 1);
     for (int i = 0; i < kKvStages; ++i) mbar_init(bar_kv + i, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_s + 1, 1);
+    mbar_init(bar_sfree, kSoftmaxThreads);
+    mbar_init(bar_sfree + 1, kSoftmaxThreads);
     mbar_init(bar_o, 1);
     mbar_init(bar_p, kSoftmaxThreads);
+    mbar_init(bar_qfree, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -154,193 +191,275 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const uint32_t tmem = *s_tmem;
   bool fail = false;
 
-  if (warp == 4) {
-    // ---- producer: one lane issues every copy and MMA ----------------------
+  if (warp >= 4) {
     if (lane == 0) {
       const uint32_t fmt = Elem<T>::code == PSB_BF16 ? 1u : 0u;
-      const uint32_t idesc_s = umma_idesc_f16(fmt, kBM, kBN, 0, 0);
-      const uint32_t idesc_o = umma_idesc_f16(fmt, kBM, kDim, 0, 1);
-      auto load_kv = [&](int t) {
-        const int st = t % kKvStages;
-        mbar_arrive_expect_tx(bar_kv + st, 2 * kKvTile);
-        tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, kvh, q0 + t * kBN, bar_kv + st);
-        tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, kvh, q0 + t * kBN, bar_kv + st);
-      };
-      // descriptors of stage 0; a k-step of 16 elements advances the
-      // address field (bytes >> 4) by 2, a K/V stage by kKvTile >> 4, a V
-      // k-step of 16 keys by 2048 >> 4
-      const uint64_t dq = umma_desc_sw128(s_base + kOffQ, 1024, 16);
-      const uint64_t dk = umma_desc_sw128(s_base + kOffK, 1024, 16);
-      const uint64_t dv = umma_desc_sw128(s_base + kOffV, 1024, 8192);
-      auto issue_qk = [&](int t) {  // K_t landed, S buffer t & 1 read by the softmax of t - 2
-        tc_fence_after();
-        const uint64_t dks = dk + static_cast<uint64_t>((t % kKvStages) * (kKvTile >> 4));
+      if (warp == 4) {
+        // ---- Q loads and S = Q K^T, one step ahead of the softmax -----------
+        const uint32_t idesc_s = umma_idesc_f16(fmt, kBM, kBN, 0, 0);
+        // descriptors of Q buffer 0 and stage 0; a k-step of 16 elements
+        // advances the address field (bytes >> 4) by 2, a Q buffer by
+        // kTile >> 4, a K/V stage by kKvTile >> 4
+        const uint64_t dq = umma_desc_sw128(s_base + kOffQ, 1024, 16);
+        const uint64_t dk = umma_desc_sw128(s_base + kOffK, 1024, 16);
+        auto load_q = [&](int k) {
+          const TileInfo ti = tile_of(k);
+          mbar_arrive_expect_tx(bar_q + (k & 1), kTile);
+          tma_load_3d(smem + kOffQ + (k & 1) * kTile, &tm_q, 0, ti.head, ti.q0 + ti.qblk * kBM, bar_q + (k & 1));
+        };
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
+        load_q(0);
+        if (my_tiles > 1) load_q(1);
+        int q_req = min(my_tiles, 2), q_seen = 0, qf_seen = 0, g = 0;
+        for (int k = 0; k < my_tiles && !fail; ++k) {
+          if (k > 0 && k + 1 < my_tiles) {
+            // Q of tile k + 1 goes into the buffer of tile k - 1, whose Q K^T is done
+            if (!mbar_wait(bar_qfree, (k - 1) & 1)) {
+              fail = true;
+              break;
+            }
+            ++qf_seen;
+            load_q(k + 1);
+            ++q_req;
+          }
+          if (!mbar_wait(bar_q + (k & 1), (k >> 1) & 1)) {
+            fail = true;
+            break;
+          }
+          ++q_seen;
+          const int n_kv = tile_of(k).n_kv;
+          const uint64_t dqs = dq + static_cast<uint64_t>((k & 1) * (kTile >> 4));
+          for (int j = 0; j < n_kv; ++j, ++g) {
+            // S buffer g & 1 held step g - 2: read by the softmax (the next phase
+            // needs this step's S, so the parity cannot alias)
+            if (g >= 2 && !mbar_wait(bar_sfree + (g & 1), ((g - 2) >> 1) & 1)) {
+              fail = true;
+              break;
+            }
+            if (!mbar_wait(bar_kv + g % kKvStages, (g / kKvStages) & 1)) {
+              fail = true;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dks = dk + static_cast<uint64_t>((g % kKvStages) * (kKvTile >> 4));
 #pragma unroll
-        for (int k = 0; k < kDim / 16; ++k)
-          umma_f16_ss(tmem + kSCol + (t & 1) * kBN, dq + 2 * k, dks + 2 * k, idesc_s, k > 0);
-        umma_commit(bar_s + (t & 1));
-      };
-      prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
-      mbar_arrive_expect_tx(bar_q, kTile);
-      tma_load_3d(smem + kOffQ, &tm_q, 0, head, q0 + qblk * kBM, bar_q);
-      int kv_req = 0, kv_seen = 0, qk_issued = 0, pv_issued = 0, pv_seen = 0, p_seen = 0;
-      for (; kv_req < min(n_kv, kKvStages - 1); ++kv_req) load_kv(kv_req);
-      bool q_ok = mbar_wait(bar_q, 0);
-      if (q_ok && mbar_wait(bar_kv, 0)) {
-        kv_seen = 1;
-        issue_qk(0);
-        qk_issued = 1;
+            for (int kk = 0; kk < kDim / 16; ++kk)
+              umma_f16_ss(tmem + kSCol + (g & 1) * kBN, dqs + 2 * kk, dks + 2 * kk, idesc_s, kk > 0);
+            umma_commit(bar_s + (g & 1));
+          }
+          if (fail) break;
+          umma_commit(bar_qfree);  // lands once every Q K^T of tile k is done
+        }
+        if (fail) {
+          flag_error(p.err, PSB_DEVERR_TIMEOUT);
+          for (int t = q_seen; t < q_req; ++t) (void)mbar_wait(bar_q + (t & 1), (t >> 1) & 1);
+          (void)qf_seen;
+        }
       } else {
-        fail = true;
-      }
-      for (int j = 0; j < n_kv && !fail; ++j) {
-        // S_{j+1}: its buffer held S_{j-1}, read by the softmax step j - 1 seen last time
-        if (j + 1 < n_kv) {
-          if (!mbar_wait(bar_kv + (j + 1) % kKvStages, ((j + 1) / kKvStages) & 1)) {
-            fail = true;
-            break;
+        // ---- K/V loads and O += P V ------------------------------------------
+        const uint32_t idesc_o = umma_idesc_f16(fmt, kBM, kDim, 0, 1);
+        // V descriptor of stage 0; a stage advances the address field by
+        // kKvTile >> 4, a k-step of 16 keys by 2048 >> 4
+        const uint64_t dv = umma_desc_sw128(s_base + kOffV, 1024, 8192);
+        TileInfo tc = tile_of(0), tn{};  // current and next tile
+        bool tn_valid = my_tiles > 1;
+        if (tn_valid) tn = tile_of(1);
+        // K/V requests run ahead through the current and the next tile
+        int rk = 0, rj = 0, rg = 0;  // tile (0 current, 1 next), step and global step of the next request
+        auto request_kv = [&](int limit_g) {
+          while (rg <= limit_g) {
+            if (rk == 1 && !tn_valid) break;
+            const TileInfo& ti = rk == 0 ? tc : tn;
+            if (rj >= ti.n_kv) {
+              if (rk == 1) break;  // tiles after the next are not known yet
+              ++rk;
+              rj = 0;
+              continue;
+            }
+            const int st = rg % kKvStages;
+            mbar_arrive_expect_tx(bar_kv + st, 2 * kKvTile);
+            tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+            tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+            ++rj;
+            ++rg;
           }
-          ++kv_seen;
-          issue_qk(j + 1);
-          ++qk_issued;
-        }
-        // softmax step j done: P_j written, S_j and O_{j-1} read
-        if (!mbar_wait(bar_p, j & 1)) {
-          fail = true;
-          break;
-        }
-        ++p_seen;
-        // P.V_{j-1} done (waited before P.V_j is issued, so the parity cannot
-        // alias): the stage of tile j - 1 is free for tile j + 3
-        if (j > 0) {
-          if (!mbar_wait(bar_o, (j - 1) & 1)) {
-            fail = true;
-            break;
-          }
-          ++pv_seen;
-        }
-        if (kv_req < n_kv && kv_req <= j + kKvStages - 1) load_kv(kv_req++);
-        tc_fence_after();
-        const uint64_t dvs = dv + static_cast<uint64_t>((j % kKvStages) * (kKvTile >> 4));
+        };
+        request_kv(kKvAhead - 1);
+        int pv_issued = 0, pv_seen = 0, g = 0;
+        for (int k = 0; k < my_tiles && !fail; ++k) {
+          const bool has_next = k + 1 < my_tiles;
+          for (int j = 0; j < tc.n_kv && !fail; ++j, ++g) {
+            // softmax step g done: P written (the next phase needs P.V of this
+            // step, so the parity cannot alias)
+            if (!mbar_wait(bar_p, g & 1)) {
+              fail = true;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dvs = dv + static_cast<uint64_t>((g % kKvStages) * (kKvTile >> 4));
 #pragma unroll
-        for (int k = 0; k < kBN / 16; ++k)
-          umma_f16_ts(tmem + kOCol, tmem + kPCol + 8 * k, dvs + 128 * k, idesc_o, j > 0 || k > 0);
-        umma_commit(bar_o);
-        ++pv_issued;
-      }
-      if (fail) {
-        flag_error(p.err, PSB_DEVERR_TIMEOUT);
-        // let copies and MMAs still in flight land before shared memory and TMEM are released
-        if (!q_ok) (void)mbar_wait(bar_q, 0);
-        for (int t = kv_seen; t < kv_req; ++t) (void)mbar_wait(bar_kv + t % kKvStages, (t / kKvStages) & 1);
-        for (int t = pv_seen; t < pv_issued; ++t) (void)mbar_wait(bar_o, t & 1);
-        (void)qk_issued;
-        (void)p_seen;
+            for (int kk = 0; kk < kBN / 16; ++kk)
+              umma_f16_ts(tmem + kOCol, tmem + kPCol + 8 * kk, dvs + 128 * kk, idesc_o, j > 0 || kk > 0);
+            umma_commit(bar_o);
+            ++pv_issued;
+            // once this P.V is done its stage takes step g + kKvAhead
+            if (!mbar_wait(bar_o, g & 1)) {
+              fail = true;
+              break;
+            }
+            ++pv_seen;
+            request_kv(g + kKvAhead);
+          }
+          if (fail) break;
+          if (has_next) {  // the next tile becomes current
+            tc = tn;
+            if (rk == 1) {
+              rk = 0;
+            } else {  // the cursor had just finished the old tile: start the new one
+              rk = 0;
+              rj = 0;
+            }
+            tn_valid = k + 2 < my_tiles;
+            if (tn_valid) tn = tile_of(k + 2);
+            // the new next tile may take requests now (P.V of step g - 1 was the last seen)
+            request_kv(g - 1 + kKvAhead);
+          }
+        }
+        if (fail) {
+          flag_error(p.err, PSB_DEVERR_TIMEOUT);
+          // let copies and MMAs still in flight land before shared memory and TMEM are released
+          for (int t = pv_seen; t < pv_issued; ++t) (void)mbar_wait(bar_o, t & 1);
+          for (int t = 0; t < kKvStages && t < rg; ++t) {
+            const int last = rg - 1 - ((rg - 1 - t) % kKvStages);  // the newest request of stage t
+            (void)mbar_wait(bar_kv + t, (last / kKvStages) & 1);
+          }
+        }
       }
     }
   } else {
     // ---- softmax warps ------------------------------------------------------
-    const int row = warp * 32 + lane;   // tile row = TMEM lane
-    const int qrow = qblk * kBM + row;  // position in the sequence
+    const int row = warp * 32 + lane;  // tile row = TMEM lane
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float sc = p.scale_log2;
-    float ms = -INFINITY, l_run = 0.f;  // row max used for the exponents (scaled by sc), row sum
-    for (int j = 0; j < n_kv && !fail; ++j) {
-      if (!mbar_wait(bar_s + (j & 1), (j >> 1) & 1)) {
-        fail = true;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[kBN];
-      tmem_ld32(t_lane + kSCol + (j & 1) * kBN, sr);
-      tmem_ld32(t_lane + kSCol + (j & 1) * kBN + 32, sr + 32);
-      tmem_wait_ld();
-      // keys past this row's position or past the sequence only occur in the last tiles
-      const int lim = min(qrow, len - 1) - j * kBN;  // last valid key column
-      const bool interior = lim >= kBN - 1;
-      float mx = -INFINITY;
-      if (interior) {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sr[c]));
-        }
-      }
-      // lazy max: move it (and rescale O and the sum) only when the row max
-      // grew by more than 2^kRescaleLog2; the warp's TMEM access is collective
-      const float mxs = mx * sc;
-      const bool grow = mxs > ms + kRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        const float ms_new = grow ? mxs : ms;
-        const float alpha = ms == -INFINITY ? 0.f : ex2_approx(ms - ms_new);  // 1 where the max stays
-        if (j > 0) {  // O holds P.V of the earlier tiles once the last of them is done
-          if (!mbar_wait(bar_o, (j - 1) & 1)) {
-            fail = true;
-            break;
-          }
-          tc_fence_after();
-          uint32_t ot[kDim];
-          tmem_ld32(t_lane + kOCol, ot);
-          tmem_ld32(t_lane + kOCol + 32, ot + 32);
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < kDim; ++d) ot[d] = __float_as_uint(__uint_as_float(ot[d]) * alpha);
-          tmem_st32(t_lane + kOCol, ot);
-          tmem_st32(t_lane + kOCol + 32, ot + 32);
-          tmem_wait_st();
-        }
-        l_run *= alpha;
-        ms = ms_new;
-      }
-      const float mu = ms == -INFINITY ? 0.f : ms;  // rows with nothing valid yet stay zero
-      float rs = 0.f;
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float x0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sc, -mu));
-        const float x1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sc, -mu));
-        rs += x0 + x1;
-        pk[c / 2] = pack2<T>(x0, x1);
-      }
-      l_run += rs;
-      // P_j overwrites P_{j-1} in TMEM: wait for P.V_{j-1} (issued right after step
-      // j - 1, so normally long done; P.V_j cannot start before this thread's
-      // arrival below, so the parity cannot alias)
-      if (j > 0) {
-        if (!mbar_wait(bar_o, (j - 1) & 1)) {
+    // output rows 16-byte aligned: whole-row vector stores
+    const bool out16 = reinterpret_cast<uintptr_t>(p.out) % 16 == 0 && p.ost % 8 == 0 && p.osh % 8 == 0;
+    int g = 0;
+    for (int k = 0; k < my_tiles && !fail; ++k) {
+      const TileInfo ti = tile_of(k);
+      const int qrow = ti.qblk * kBM + row;  // position in the sequence
+      float ms = -INFINITY, l_run = 0.f;     // row max used for the exponents (scaled by sc), row sum
+      for (int j = 0; j < ti.n_kv; ++j, ++g) {
+        if (!mbar_wait(bar_s + (g & 1), (g >> 1) & 1)) {
           fail = true;
           break;
         }
+        tc_fence_after();
+        uint32_t sr[kBN];
+        tmem_ld32(t_lane + kSCol + (g & 1) * kBN, sr);
+        tmem_ld32(t_lane + kSCol + (g & 1) * kBN + 32, sr + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar_sfree + (g & 1));  // the S buffer may take step g + 2
+        // keys past this row's position or past the sequence only occur in the last steps
+        const int lim = min(qrow, ti.len - 1) - j * kBN;  // last valid key column
+        float mx = -INFINITY;
+        if (lim >= kBN - 1) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, __uint_as_float(sr[c]));
+          }
+        }
+        // lazy max: move it (and rescale O and the sum) only when the row max
+        // grew by more than 2^kRescaleLog2; the warp's TMEM access is collective
+        const float mxs = mx * sc;
+        const bool grow = mxs > ms + kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float ms_new = grow ? mxs : ms;
+          const float alpha = ms == -INFINITY ? 0.f : ex2_approx(ms - ms_new);  // 1 where the max stays
+          if (j > 0) {  // O holds P.V of the earlier steps once the last of them is done
+            if (!mbar_wait(bar_o, (g - 1) & 1)) {
+              fail = true;
+              break;
+            }
+            tc_fence_after();
+            uint32_t ot[kDim];
+            tmem_ld32(t_lane + kOCol, ot);
+            tmem_ld32(t_lane + kOCol + 32, ot + 32);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < kDim; ++d) ot[d] = __float_as_uint(__uint_as_float(ot[d]) * alpha);
+            tmem_st32(t_lane + kOCol, ot);
+            tmem_st32(t_lane + kOCol + 32, ot + 32);
+            tmem_wait_st();
+          }
+          l_run *= alpha;
+          ms = ms_new;
+        }
+        const float mu = ms == -INFINITY ? 0.f : ms;  // rows with nothing valid yet stay zero
+        float rs = 0.f;
+        uint32_t pk[kBN / 2];
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) {
+          const float x0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sc, -mu));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sc, -mu));
+          rs += x0 + x1;
+          pk[c / 2] = pack2<T>(x0, x1);
+        }
+        l_run += rs;
+        // P overwrites the previous step's P in TMEM: wait for that P.V (issued
+        // right after the previous step, so normally long done; the next P.V
+        // cannot start before this thread's arrival below, so the parity cannot alias)
+        if (g > 0) {
+          if (!mbar_wait(bar_o, (g - 1) & 1)) {
+            fail = true;
+            break;
+          }
+        }
+        tmem_st32(t_lane + kPCol, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p);
       }
-      tmem_st32(t_lane + kPCol, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar_p);
-    }
-    if (!fail && !mbar_wait(bar_o, (n_kv - 1) & 1)) fail = true;  // the last P.V
-    if (fail) {
-      if (lane == 0) flag_error(p.err, PSB_DEVERR_TIMEOUT);
-    } else {
+      if (fail) break;
+      // the tile's last P.V, then its output (before this thread's arrival for
+      // the next tile's first step lets the producer overwrite O)
+      if (!mbar_wait(bar_o, (g - 1) & 1)) {
+        fail = true;
+        break;
+      }
       tc_fence_after();
       uint32_t ot[kDim];
       tmem_ld32(t_lane + kOCol, ot);
       tmem_ld32(t_lane + kOCol + 32, ot + 32);
       tmem_wait_ld();
-      if (qrow < len && q0 + qrow < p.total) {
+      tc_fence_before();
+      if (qrow < ti.len && ti.q0 + qrow < p.total) {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        T* op = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(q0 + qrow) * p.ost +
-                static_cast<int64_t>(head) * p.osh;
+        T* op = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(ti.q0 + qrow) * p.ost +
+                static_cast<int64_t>(ti.head) * p.osh;
+        if (out16) {
 #pragma unroll
-        for (int d = 0; d < kDim; d += 2)
-          *reinterpret_cast<uint32_t*>(op + d) =
-              pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
+          for (int d = 0; d < kDim; d += 8)
+            *reinterpret_cast<uint4*>(op + d) =
+                make_uint4(pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 2]) * inv, __uint_as_float(ot[d + 3]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 4]) * inv, __uint_as_float(ot[d + 5]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 6]) * inv, __uint_as_float(ot[d + 7]) * inv));
+        } else {
+#pragma unroll
+          for (int d = 0; d < kDim; d += 2)
+            *reinterpret_cast<uint32_t*>(op + d) =
+                pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
+        }
       }
     }
+    if (fail && lane == 0) flag_error(p.err, PSB_DEVERR_TIMEOUT);
   }
   tc_fence_before();
   __syncthreads();
@@ -350,7 +469,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   }
 }
 
-size_t tc_smem_bytes(int max_level) { return 1024 + kSmemTiles + 88 + sizeof(int32_t) * (max_level + 2); }
+size_t tc_smem_bytes(int max_level, int num_seqs) {
+  return 1024 + kSmemTiles + kSmemBars + sizeof(int32_t) * (3 * (static_cast<size_t>(max_level) + 1) + num_seqs);
+}
 
 }  // namespace
 
@@ -362,7 +483,7 @@ bool prefill_tc_supported(const PrefillParams& p, int dtype) {
                        p.vsh % 8 == 0 && p.ost % 2 == 0 && p.osh % 2 == 0 && p.qst > 0 && p.kst > 0 && p.vst > 0;
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
   return strides && al16(p.q) && al16(p.k) && al16(p.v) && reinterpret_cast<uintptr_t>(p.out) % 4 == 0 &&
-         max_level <= kMaxLevels && tc_smem_bytes(max_level) <= 227 * 1024;
+         max_level <= kMaxLevels && p.num_seqs <= kMaxTcSeqs && tc_smem_bytes(max_level, p.num_seqs) <= 227 * 1024;
 }
 
 int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
@@ -373,16 +494,18 @@ int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
       !encode_rows_map(&tv, p.v, p.total, p.hkv, kDim, p.vst, p.vsh, kBN, dt))
     return PSB_ERR_CUDA;
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
-  // an upper bound of the tiles: sum over sequences of ceil(len / 128)
-  const int64_t tiles = static_cast<int64_t>(p.total) / kBM + p.num_seqs;
-  const int64_t grid = tiles * p.hq;
-  if (grid == 0) return PSB_OK;
-  if (grid >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
-  const size_t smem = tc_smem_bytes(max_level);
+  // an upper bound of the tiles: sum over sequences of ceil(len / 128), times the heads
+  const int64_t tiles = (static_cast<int64_t>(p.total) / kBM + p.num_seqs) * p.hq;
+  if (tiles == 0) return PSB_OK;
+  if (tiles >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
+  const size_t smem = tc_smem_bytes(max_level, p.num_seqs);
   const void* kern = dtype == PSB_BF16 ? reinterpret_cast<const void*>(prefill_tc_kernel<__nv_bfloat16>)
                                        : reinterpret_cast<const void*>(prefill_tc_kernel<__half>);
   int occ = 0;
   if (!kernel_occupancy(kern, kTcThreads, smem, &occ) || occ < 1) return PSB_ERR_CUDA;
+  const int sms = device_sm_count();
+  if (sms <= 0) return PSB_ERR_CUDA;
+  const int64_t grid = std::min<int64_t>(tiles, static_cast<int64_t>(sms) * occ);  // persistent
   discard_stale_error();
   cudaError_t e;
   if (dtype == PSB_BF16)
