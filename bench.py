@@ -42,6 +42,9 @@ HQ, HKV, D, BS, SLACK, POOL_LAYERS = 14, 2, 64, 16, 1.25, 4
 METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s); decode tok/s at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+# DRAM bytes of one decode + combine launch on the rank-0 workload, measured with ncu
+DECODE_TRAFFIC_BYTES = 198_700_000
 
 
 def context_lengths(seed: int) -> np.ndarray:
@@ -69,6 +72,118 @@ def load_peaks() -> tuple[float, str]:
             return float(json.load(fh)["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_tensor_peak() -> tuple[float, str]:
+    """bf16 dense TFLOP/s of a burst (the prefill kernel is timed on its own)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+PREFILL_TOKENS, PREFILL_MEDIAN, PREFILL_SIGMA, PREFILL_LO, PREFILL_HI, PREFILL_PACKS = 16384, 256, 1.0, 32, 2048, 4
+
+
+def prefill_lengths(seed: int) -> list[int]:
+    """Prompts lognormal(median 256, sigma 1.0) clipped to [32, 2048], packed up to 16384 tokens."""
+    rng = np.random.default_rng(seed)
+    lens = []
+    while True:
+        n = int(np.clip(round(rng.lognormal(math.log(PREFILL_MEDIAN), PREFILL_SIGMA)), PREFILL_LO, PREFILL_HI))
+        if sum(lens) + n > PREFILL_TOKENS:
+            return lens
+        lens.append(n)
+
+
+def prefill_flops(lens) -> float:
+    """Causal attention FLOPs: 2 matmuls x 2 flop x Hq x D x L (L + 1) / 2 per sequence."""
+    return float(sum(4 * HQ * D * n * (n + 1) / 2 for n in lens))
+
+
+def run_prefill(args, device, seed: int) -> dict:
+    """Packed causal prefill with the paged KV write of one engine iteration
+    (varlen_prefill + reshape_and_cache of every prompt token), on PREFILL_PACKS
+    different packs in turn so consecutive steps do not run from L2."""
+    from pagedserve_b200 import ops
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    packs = []
+    for i in range(PREFILL_PACKS):
+        lens = prefill_lengths(seed + i)
+        t = sum(lens)
+        need = sum(-(-n // BS) for n in lens)
+        nb = int(math.ceil(SLACK * need))
+        perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + i))[:need]
+        slots, at = [], 0
+        for n in lens:
+            k = -(-n // BS)
+            blocks = perm[at:at + k]
+            at += k
+            pos = torch.arange(n)
+            slots.append(blocks[pos // BS] * BS + pos % BS)
+        packs.append(dict(
+            lens=lens, q=torch.randn(t, HQ, D, device=device, dtype=torch.bfloat16, generator=gen),
+            k=torch.randn(t, HKV, D, device=device, dtype=torch.bfloat16, generator=gen),
+            v=torch.randn(t, HKV, D, device=device, dtype=torch.bfloat16, generator=gen),
+            cu=torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=device),
+            slots=torch.cat(slots).to(device=device, dtype=torch.int64),
+            kc=torch.empty(1, nb, HKV, BS, D, device=device, dtype=torch.bfloat16),
+            vc=torch.empty(1, nb, HKV, BS, D, device=device, dtype=torch.bfloat16),
+            out=torch.empty(t, HQ, D, device=device, dtype=torch.bfloat16)))
+
+    def step(pk, attn=True, write=True):
+        if write:
+            ops.reshape_and_cache(pk["k"], pk["v"], pk["kc"], pk["vc"], pk["slots"], 0)
+        if attn:
+            ops.varlen_prefill(pk["q"], pk["k"], pk["v"], pk["cu"], max(pk["lens"]), out=pk["out"])
+
+    stream = torch.cuda.Stream(device)
+    graphs, attn_graphs = [], []
+    with torch.cuda.stream(stream):
+        for pk in packs:
+            step(pk)
+        torch.cuda.synchronize()
+        for pk in packs:
+            for lst, kw in ((graphs, {}), (attn_graphs, {"write": False})):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(pk, **kw)
+                lst.append(g)
+    torch.cuda.synchronize()
+
+    def timed(gs):
+        for i in range(args.warmup):
+            gs[i % PREFILL_PACKS].replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(args.steps):
+            gs[i % PREFILL_PACKS].replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    step_ms, attn_ms = timed(graphs), timed(attn_graphs)
+    for g in graphs + attn_graphs:
+        g.reset()
+    flops = statistics.mean(prefill_flops(pk["lens"]) for pk in packs)
+    tokens = statistics.mean(sum(pk["lens"]) for pk in packs)
+    peak, kind = load_tensor_peak()
+    tflops = flops / (attn_ms * 1e-3) / 1e12
+    return {
+        "workload": "packed causal prefill + paged KV write: prompts lognormal(median 256, sigma 1.0) clipped "
+                    "[32, 2048], packed to <= 16384 tokens, 14q/2kv heads, d64, block 16, bf16; "
+                    f"{PREFILL_PACKS} packs in turn",
+        "seqs_per_pack": [len(pk["lens"]) for pk in packs], "tokens_per_pack": tokens,
+        "ms_per_step": round(step_ms, 5), "attn_layer_tokens_per_s": round(tokens / (step_ms * 1e-3), 1),
+        "attention": {"kernel": "prefill_tc_kernel (tcgen05/TMEM, TMA)", "ms": round(attn_ms, 5),
+                      "gflop": round(flops / 1e9, 3), "tflops": round(tflops, 1), "peak_tflops": peak,
+                      "peak_kind": kind, "frac": round(tflops / peak, 4), "bound": "tensor"},
+        "gpu_launches_per_step": 2,
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -358,6 +473,9 @@ def run_b200(args, world, rank, local):
     h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + 8 * BATCH + 4 * BATCH * (width + 1)
     d2h = o_host.numel() * 2
 
+    # ---- packed prefill (one engine iteration's attention and KV write) ------
+    prefill = run_prefill(args, device, 2000 + rank)
+
     # ---- reduce over ranks --------------------------------------------------
     local_stats = torch.tensor([step_ms, dec_ms, e2e_ms], dtype=torch.float64, device=device)
     if pg is not None:
@@ -393,12 +511,16 @@ def run_b200(args, world, rank, local):
                          "kernel": "decode_fast_kernel<bf16, 2> + decode_combine_kernel",
                          "timing": "CUDA events around each decode+combine graph replay, K replays",
                          "bytes_per_launch": decode_bytes(lens),
-                         "avg_launch_ms": round(dec_ms, 5), "traffic": None},
+                         "avg_launch_ms": round(dec_ms, 5), "traffic": DECODE_TRAFFIC_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode "
+                                           "(193.9 MB) and one combine (4.8 MB) launch on this seeded workload "
+                                           "(decode ncu summary under profiles/)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
                     "path": "paged_decode_attention + write_tokens (reference-facing API), pinned host buffers"},
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),
+            "prefill": prefill,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
