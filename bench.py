@@ -13,9 +13,11 @@ of KV that is not resident in the 126 MB L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Under torchrun every rank runs its own 256-sequence batch on its own GPU
-(requests shard by sequence, no collective on the data path: weak scaling);
-the step time is the max over ranks.  ``--impl reference`` times the
+Under torchrun with N ranks, N x 256 requests are drawn and placed on the
+GPUs in arrival order by ``SequenceDispatcher`` (the rank with the most free
+KV blocks takes the next request); each rank serves its shard from its own
+pool, with no collective on the data path (weak scaling).  The step time is
+the max over ranks and the bytes are summed over ranks.  ``--impl reference`` times the
 reference algorithm's CPU restatement (the oracle) on the host cores instead.
 """
 
@@ -47,9 +49,21 @@ FALLBACK_BF16_TFLOPS = 1590.0
 DECODE_TRAFFIC_BYTES = 198_700_000
 
 
-def context_lengths(seed: int) -> np.ndarray:
+def context_lengths(seed: int, n: int = BATCH) -> np.ndarray:
     rng = np.random.default_rng(seed)
-    return np.clip(np.round(rng.lognormal(math.log(MEDIAN), SIGMA, BATCH)), LO, HI).astype(np.int64)
+    return np.clip(np.round(rng.lognormal(math.log(MEDIAN), SIGMA, n)), LO, HI).astype(np.int64)
+
+
+def rank_lengths(world: int, rank: int) -> np.ndarray:
+    """This rank's contexts: world x 256 requests drawn once, placed on the
+    ranks in arrival order by ``SequenceDispatcher`` (most free KV blocks
+    first).  At one GPU this is the plain 256-sequence batch."""
+    from pagedserve_b200.sharding import shard_sequences
+    lens = context_lengths(1000, BATCH * world)
+    if world == 1:
+        return lens
+    blocks = int(math.ceil(SLACK * np.sum(-(-lens // BS)) / world))
+    return lens[shard_sequences(lens, world, blocks, BS)[rank]]
 
 
 def decode_bytes(lens: np.ndarray) -> int:
@@ -326,15 +340,16 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def build_device_workload(seed: int, device: torch.device):
+def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | None = None):
     from pagedserve_b200 import PagedKVCache
     rng = np.random.default_rng(seed + 7)
-    lens = context_lengths(seed)
+    lens = context_lengths(seed) if lens is None else lens
+    batch = len(lens)
     need = int(np.sum(-(-lens // BS)))
     nb = int(math.ceil(SLACK * need))
     cache = PagedKVCache(num_blocks=nb, num_layers=POOL_LAYERS, num_kv_heads=HKV, head_dim=D, block_size=BS,
                          dtype=torch.bfloat16, device=device, free_order=rng.permutation(nb))
-    ids = [f"seq-{i}" for i in range(BATCH)]
+    ids = [f"seq-{i}" for i in range(batch)]
     for rid, n in zip(ids, lens):
         cache.allocate(rid, int(n))
     gen = torch.Generator(device=device)
@@ -345,9 +360,9 @@ def build_device_workload(seed: int, device: torch.device):
     tables = torch.from_numpy(cache.table_rows(ids)).to(device)
     lens_t = torch.from_numpy(lens.astype(np.int32)).to(device)
     slots = torch.tensor([cache.slot_of(r, p) for r, p in zip(ids, positions)], dtype=torch.int64, device=device)
-    q = torch.randn(BATCH, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
-    new_k = torch.randn(BATCH, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
-    new_v = torch.randn(BATCH, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    q = torch.randn(batch, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
+    new_k = torch.randn(batch, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    new_v = torch.randn(batch, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
     return dict(cache=cache, ids=ids, positions=positions, lens=lens, tables=tables, lens_t=lens_t, slots=slots,
                 q=q, new_k=new_k, new_v=new_v)
 
@@ -363,7 +378,8 @@ def run_b200(args, world, rank, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         pg = dist
 
-    w = build_device_workload(1000 + rank, device)
+    w = build_device_workload(1000 + rank, device, rank_lengths(world, rank))
+    batch = len(w["lens"])
     k, v = w["cache"].kv_cache.k_cache, w["cache"].kv_cache.v_cache
     out = torch.empty_like(w["q"])
     err = torch.zeros(1, dtype=torch.int32, device=device)
@@ -444,7 +460,7 @@ def run_b200(args, world, rank, local):
     q_host = w["q"].cpu().pin_memory()
     k_host = w["new_k"].cpu().pin_memory()
     v_host = w["new_v"].cpu().pin_memory()
-    o_host = torch.empty((BATCH, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
+    o_host = torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
     h2d_box = {}
 
     def e2e_step(s):
@@ -470,23 +486,25 @@ def run_b200(args, world, rank, local):
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     width = cache.table_rows(ids).shape[1]
-    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + 8 * BATCH + 4 * BATCH * (width + 1)
+    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + 8 * batch + 4 * batch * (width + 1)
     d2h = o_host.numel() * 2
 
     # ---- packed prefill (one engine iteration's attention and KV write) ------
     prefill = run_prefill(args, device, 2000 + rank)
 
-    # ---- reduce over ranks --------------------------------------------------
-    local_stats = torch.tensor([step_ms, dec_ms, e2e_ms], dtype=torch.float64, device=device)
-    if pg is not None:
-        pg.all_reduce(local_stats, op=pg.ReduceOp.MAX)
-    step_ms, dec_ms, e2e_ms = (float(x) for x in local_stats.tolist())
+    # ---- reduce over ranks: times by max, work by sum ------------------------
+    from pagedserve_b200.sharding import aggregate_counters
     lens = w["lens"]
-    step_bytes = decode_bytes(lens) + reshape_bytes(BATCH)
-    value = step_bytes * world / (step_ms * 1e-3) / 1e9
-    e2e_value = step_bytes * world / (e2e_ms * 1e-3) / 1e9
+    step_bytes = decode_bytes(lens) + reshape_bytes(batch)
+    rank_dec_ms = dec_ms
+    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms}, device, op="max")
+    work = aggregate_counters({"bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())}, device, op="sum")
+    step_ms, dec_ms, e2e_ms = times["step_ms"], times["dec_ms"], times["e2e_ms"]
+    total_bytes, total_seqs = work["bytes"], int(work["seqs"])
+    value = total_bytes / (step_ms * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
-    achieved = decode_bytes(lens) / (dec_ms * 1e-3) / 1e9
+    achieved = decode_bytes(lens) / (rank_dec_ms * 1e-3) / 1e9
 
     if rank == 0:
         cpu = cpu_baseline(0) if world == 1 else None
@@ -494,10 +512,12 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) KV/Q, lognormal contexts)",
-            "config": {"workload": "serving-scale paged decode + reshape_and_cache: 256 seqs/GPU, ctx lognormal("
-                                   "median 1024, sigma 0.8) clipped [16, 8192], 14q/2kv heads, d64, block 16, "
-                                   "pool 1.25x need, shuffled blocks",
-                       "sum_ctx_per_gpu": int(lens.sum()), "bytes_per_step_per_gpu": step_bytes,
+            "config": {"workload": "serving-scale paged decode + reshape_and_cache: 256 x N_gpus requests, ctx "
+                                   "lognormal(median 1024, sigma 0.8) clipped [16, 8192], placed on the GPUs in "
+                                   "arrival order by most free KV blocks; 14q/2kv heads, d64, block 16, pool 1.25x "
+                                   "need per GPU, shuffled blocks",
+                       "sequences": total_seqs, "sum_ctx": int(work["ctx"]), "bytes_per_step": int(total_bytes),
+                       "rank0_sequences": batch, "rank0_sum_ctx": int(lens.sum()),
                        "l2": "inputs larger than L2: 4-layer pool, consecutive steps use different layers "
                              "(~180 MB KV each)",
                        "launch": "one CUDA graph per step (reshape_and_cache, decode, split-K combine; "
@@ -505,7 +525,7 @@ def run_b200(args, world, rank, local):
                        "parallelism": f"sequence-sharded x{world}"},
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
-            "attn_layer_tok_per_s": round(BATCH * world / (step_ms * 1e-3), 1),
+            "attn_layer_tok_per_s": round(total_seqs / (step_ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "decode_fast_kernel<bf16, 2> + decode_combine_kernel",

@@ -9,12 +9,15 @@ Public surface:
   tensor-level API over the C ABI (include/pagedserve_b200.h)
 * ``PagedKVCache`` and friends - host-side block bookkeeping with the
   reference's interface
+* ``SequenceDispatcher`` - places requests on the GPUs of a node (one
+  process and one KV pool per GPU, no collective on the attention path)
 """
 
 from . import ops
 from .attention import paged_decode_attention, write_tokens
 from .paged_kv import BlockManager, BlockTable, KVCache, PagedKVCache
+from .sharding import SequenceDispatcher
 
 __all__ = ["ops", "paged_decode_attention", "write_tokens", "BlockManager", "BlockTable", "KVCache",
-           "PagedKVCache"]
+           "PagedKVCache", "SequenceDispatcher"]
 __version__ = "0.1.0"

@@ -347,21 +347,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// 2^x for x <= ~8 on the FMA pipe, so part of a softmax's exponentials can
-// leave the special-function unit: round-to-nearest range reduction
-// x = n + f, f in [-0.5, 0.5] (the 1.5 * 2^23 addition leaves n in the low
-// mantissa bits), 2^f by a cubic fitted here by iteratively reweighted least
-// squares for minimal relative error (7.5e-5 on [-0.5, 0.5]), and 2^n added
-// to the exponent field.  Inputs below -126 give 2^-126.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05517150f, f, 0.24261096f), f, 0.69326097f), f, 0.99992806f);
-  const int n = __float_as_int(t) - __float_as_int(12582912.f);
-  return __int_as_float(__float_as_int(p) + static_cast<int>(static_cast<unsigned>(n) << 23));
-}
-
 // 32 lanes x 32 bit, 32 consecutive columns per thread, followed by the
 // wait in the same asm statement so no use of the registers can be scheduled
 // before the data has landed.
