@@ -7,9 +7,10 @@ Workload (one "step" = one layer call of the decode hot path over one batch):
 64), block_size 16, bf16; physical blocks shuffled across a pool of 1.25x
 the need; the step writes one new token per sequence through a slot mapping
 (reshape_and_cache) and runs split-K paged decode attention over the pool.
-Synthetic seeded data (no dataset or weights are involved).  Consecutive
-steps use different layers of a 4-layer pool, so every step streams ~180 MB
-of KV that is not resident in the 126 MB L2.
+Synthetic seeded data (no dataset or weights are involved).  The pool holds
+the model's 24 layers and consecutive steps are consecutive layers, so every
+step streams ~180 MB of KV that is not resident in the 126 MB L2.  Steps run
+as the decode iteration runs them: one CUDA graph holds the 24 layer calls.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -17,8 +18,9 @@ Under torchrun with N ranks, N x 256 requests are drawn and placed on the
 GPUs in arrival order by ``SequenceDispatcher`` (the rank with the most free
 KV blocks takes the next request); each rank serves its shard from its own
 pool, with no collective on the data path (weak scaling).  The step time is
-the max over ranks and the bytes are summed over ranks.  ``--impl reference`` times the
-reference algorithm's CPU restatement (the oracle) on the host cores instead.
+the max over ranks and the bytes are summed over ranks.  ``--impl reference``
+times the reference algorithm's CPU restatement (the oracle) on the host
+cores instead.
 """
 
 from __future__ import annotations
@@ -40,7 +42,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 BATCH, MEDIAN, SIGMA, LO, HI = 256, 1024, 0.8, 16, 8192
-HQ, HKV, D, BS, SLACK, POOL_LAYERS = 14, 2, 64, 16, 1.25, 4
+HQ, HKV, D, BS, SLACK = 14, 2, 64, 16, 1.25
+LAYERS = 24  # Qwen2.5-0.5B decoder layers: one decode iteration is 24 layer calls
 METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s); decode tok/s at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
@@ -347,7 +350,7 @@ def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | No
     batch = len(lens)
     need = int(np.sum(-(-lens // BS)))
     nb = int(math.ceil(SLACK * need))
-    cache = PagedKVCache(num_blocks=nb, num_layers=POOL_LAYERS, num_kv_heads=HKV, head_dim=D, block_size=BS,
+    cache = PagedKVCache(num_blocks=nb, num_layers=LAYERS, num_kv_heads=HKV, head_dim=D, block_size=BS,
                          dtype=torch.bfloat16, device=device, free_order=rng.permutation(nb))
     ids = [f"seq-{i}" for i in range(batch)]
     for rid, n in zip(ids, lens):
@@ -390,68 +393,77 @@ def run_b200(args, world, rank, local):
     def decode(layer):
         ops.paged_decode(w["q"], k, v, w["tables"], w["lens_t"], layer, out=out, error_flag=err)
 
-    for layer in range(POOL_LAYERS):  # warm the library, size the workspace
+    for layer in range(LAYERS):  # warm the library, size the workspace
         reshape(layer)
         decode(layer)
     torch.cuda.synchronize()
 
-    # One CUDA graph per layer holding the whole step (reshape_and_cache, then
-    # decode and its split-K combine, which start under their predecessor via
-    # programmatic dependent launch), and one holding only decode + combine
-    # for the kernel-level roofline timing.
+    # One CUDA graph per decode iteration: the 24 layers' attention calls in
+    # order, each reshape_and_cache then decode + split-K combine, chained by
+    # programmatic dependent launch.  A step is one layer call: K steps are
+    # K // 24 iteration graphs plus one graph of the first K % 24 layers.
+    # Decode-only graphs of the same shape time the kernel for the roofline,
+    # and one graph per layer call shows the cost of launching each alone.
     stream = torch.cuda.Stream(device)
-    g_step, g_dec = [], []
+
+    def capture(layers, with_reshape=True):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for layer in layers:
+                if with_reshape:
+                    reshape(layer)
+                decode(layer)
+        return g
+
+    full, rem = divmod(args.steps, LAYERS)
     with torch.cuda.stream(stream):
-        for layer in range(POOL_LAYERS):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                reshape(layer)
-                decode(layer)
-            g_step.append(g)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                decode(layer)
-            g_dec.append(g)
+        g_iter = capture(range(LAYERS))
+        g_rem = capture(range(rem)) if rem else None
+        g_dec_iter = capture(range(LAYERS), with_reshape=False)
+        g_dec_rem = capture(range(rem), with_reshape=False) if rem else None
+        g_single = [capture([layer]) for layer in range(LAYERS)]
     torch.cuda.synchronize()
 
-    for s in range(args.warmup):
-        g_step[s % POOL_LAYERS].replay()
-        g_dec[s % POOL_LAYERS].replay()
+    def run_steps(g_all, g_part):
+        for _ in range(full):
+            g_all.replay()
+        if g_part is not None:
+            g_part.replay()
+
+    for _ in range(-(-args.warmup // LAYERS)):  # at least W warm-up layer calls of each kind
+        g_iter.replay()
+        g_dec_iter.replay()
+    for g in g_single:
+        g.replay()
     torch.cuda.synchronize()
 
     def barrier():
         if pg is not None:
             pg.barrier()
 
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def timed(fn):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        t0.record()
+        fn()
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return t0.elapsed_time(t1)
+
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
     gpu_ids = [int(x) for x in visible.split(",")][:max(world, 1)] if visible else list(range(max(world, 1)))
     clocks = Clocks(gpu_ids if rank == 0 else [])
     if rank == 0:
         clocks.__enter__()
-    barrier()
-    torch.cuda.synchronize()
-    t_start.record()
-    for s in range(args.steps):
-        g_step[s % POOL_LAYERS].replay()
-    t_end.record()
-    torch.cuda.synchronize()
-    barrier()
-    step_ms = t_start.elapsed_time(t_end) / args.steps
-    # the decode kernel alone (decode + split-K combine), same K, same layer rotation
-    dec_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
-    for s in range(args.steps):
-        dec_events[s][0].record()
-        g_dec[s % POOL_LAYERS].replay()
-        dec_events[s][1].record()
-    torch.cuda.synchronize()
-    barrier()
+    step_ms = timed(lambda: run_steps(g_iter, g_rem)) / args.steps
+    # the decode kernel alone (decode + split-K combine), same K layer calls
+    dec_ms = timed(lambda: run_steps(g_dec_iter, g_dec_rem)) / args.steps
+    # the same layer calls, one graph launch each
+    single_ms = timed(lambda: [g_single[s % LAYERS].replay() for s in range(args.steps)]) / args.steps
     if rank == 0:
         clocks.__exit__(None, None, None)
-    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec_events)
     if int(err.item()) != 0:
         raise RuntimeError(f"device error flag {int(err.item())}")
 
@@ -461,10 +473,13 @@ def run_b200(args, world, rank, local):
     k_host = w["new_k"].cpu().pin_memory()
     v_host = w["new_v"].cpu().pin_memory()
     o_host = torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
-    h2d_box = {}
+
+    from pagedserve_b200.attention import clear_metadata_cache
 
     def e2e_step(s):
-        layer = s % POOL_LAYERS
+        layer = s % LAYERS
+        if layer == 0:  # a new decode iteration: block tables and slots are rebuilt and copied once
+            clear_metadata_cache(cache)
         qd = q_host.to(device, non_blocking=True).unsqueeze(2)  # [B, Hq, 1, D]
         kd = k_host.to(device, non_blocking=True)
         vd = v_host.to(device, non_blocking=True)
@@ -486,7 +501,9 @@ def run_b200(args, world, rank, local):
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     width = cache.table_rows(ids).shape[1]
-    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + 8 * batch + 4 * batch * (width + 1)
+    iterations = -(-args.steps // LAYERS)  # metadata copies inside the timed region
+    meta_bytes = 8 * batch + 4 * batch * (width + 1)  # slots; table + lengths
+    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + meta_bytes * iterations / args.steps
     d2h = o_host.numel() * 2
 
     # ---- packed prefill (one engine iteration's attention and KV write) ------
@@ -497,9 +514,10 @@ def run_b200(args, world, rank, local):
     lens = w["lens"]
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
     rank_dec_ms = dec_ms
-    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms}, device, op="max")
+    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms},
+                               device, op="max")
     work = aggregate_counters({"bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())}, device, op="sum")
-    step_ms, dec_ms, e2e_ms = times["step_ms"], times["dec_ms"], times["e2e_ms"]
+    step_ms, dec_ms, e2e_ms, single_ms = times["step_ms"], times["dec_ms"], times["e2e_ms"], times["single_ms"]
     total_bytes, total_seqs = work["bytes"], int(work["seqs"])
     value = total_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
@@ -518,10 +536,13 @@ def run_b200(args, world, rank, local):
                                    "need per GPU, shuffled blocks",
                        "sequences": total_seqs, "sum_ctx": int(work["ctx"]), "bytes_per_step": int(total_bytes),
                        "rank0_sequences": batch, "rank0_sum_ctx": int(lens.sum()),
-                       "l2": "inputs larger than L2: 4-layer pool, consecutive steps use different layers "
-                             "(~180 MB KV each)",
-                       "launch": "one CUDA graph per step (reshape_and_cache, decode, split-K combine; "
-                                 "programmatic dependent launch between them)",
+                       "l2": "inputs larger than L2: a 24-layer pool, consecutive steps are consecutive "
+                             "layers (~180 MB of KV each, read with an evict-first L2 policy)",
+                       "launch": "one CUDA graph per decode iteration: 24 layer calls, each reshape_and_cache "
+                                 "then decode + split-K combine, chained by programmatic dependent launch; a "
+                                 "step is one layer call",
+                       "per_layer_graph_ms": round(single_ms, 5),
+                       "per_layer_graph_note": "the same layer calls launched as one CUDA graph each",
                        "parallelism": f"sequence-sharded x{world}"},
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
@@ -529,7 +550,8 @@ def run_b200(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "decode_fast_kernel<bf16, 2> + decode_combine_kernel",
-                         "timing": "CUDA events around each decode+combine graph replay, K replays",
+                         "timing": "CUDA events around K decode+combine layer calls in decode-only iteration "
+                                   "graphs; average per layer call",
                          "bytes_per_launch": decode_bytes(lens),
                          "avg_launch_ms": round(dec_ms, 5), "traffic": DECODE_TRAFFIC_BYTES,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode "
@@ -537,16 +559,20 @@ def run_b200(args, world, rank, local):
                                            "(decode ncu summary under profiles/)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
-                    "path": "paged_decode_attention + write_tokens (reference-facing API), pinned host buffers"},
+                    "path": "per layer call: q, new k, new v copied from pinned host buffers, write_tokens + "
+                            "paged_decode_attention (reference-facing API), output copied back; block tables "
+                            "and slots built and copied once per 24-layer iteration"},
             "gpu_launches": 3 * args.steps,
+            "gpu_launches_note": "per step: reshape_and_cache, decode, combine",
             "clocks": clocks.summary(),
             "prefill": prefill,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    for g in g_step + g_dec:
-        g.reset()
+    for g in [g_iter, g_rem, g_dec_iter, g_dec_rem] + g_single:
+        if g is not None:
+            g.reset()
     if pg is not None:
         pg.destroy_process_group()
 

@@ -13,10 +13,19 @@ attention runs in the sm_100a split-K kernel of ``libpagedserve_b200.so``.
 ``write_tokens`` replaces the per-row ``write_token`` loop
 (pagedserve/attention/batched_paged_attention.py:115-124) with one
 ``reshape_and_cache`` launch.
+
+The reference rebuilds the table for every layer of every decode iteration
+(triton_paged_decode.py:134-154) although all layers of one iteration see the
+same requests, positions and blocks.  With this package's ``PagedKVCache``,
+whose ``metadata_epoch`` changes on every allocation, growth or release, the
+device copies (table, lengths, slots) are kept on the cache object and reused
+while the epoch, the request ids and the positions are unchanged; any other
+cache object is rebuilt on every call, as in the reference.
 """
 
 from __future__ import annotations
 
+from collections import OrderedDict
 from collections.abc import Sequence
 
 import numpy as np
@@ -25,11 +34,47 @@ import torch
 from . import ops
 
 
+_KEEP = 4  # metadata entries kept per cache (one per live batch shape)
+
+
+def _memo(cache, kind: str, request_ids, positions, device, build):
+    """``build()``, or its result from an earlier call at the same cache
+    epoch for the same requests, positions and device."""
+    epoch = getattr(cache, "metadata_epoch", None)
+    if epoch is None:
+        return build()
+    store = getattr(cache, "_psb_metadata", None)
+    if store is None:
+        store = cache._psb_metadata = OrderedDict()
+    key = (kind, epoch, tuple(request_ids), tuple(int(p) for p in positions), str(device))
+    hit = store.get(key)
+    if hit is not None:
+        store.move_to_end(key)
+        return hit
+    value = build()
+    store[key] = value
+    while len(store) > _KEEP:
+        store.popitem(last=False)
+    return value
+
+
+def clear_metadata_cache(cache) -> None:
+    """Drop the device copies of block tables and slots kept on ``cache``."""
+    store = getattr(cache, "_psb_metadata", None)
+    if store is not None:
+        store.clear()
+
+
 def _host_metadata(cache, request_ids, positions, device):
     """(table [B, M] int32, lengths [B] int32) as one device tensor pair.
 
     Raises the reference's position error (triton_paged_decode.py:134-141).
     """
+    return _memo(cache, "table", request_ids, positions, device,
+                 lambda: _build_metadata(cache, request_ids, positions, device))
+
+
+def _build_metadata(cache, request_ids, positions, device):
     lengths = np.empty(len(request_ids), dtype=np.int32)
     tables = []
     for row, (rid, pos) in enumerate(zip(request_ids, positions)):
@@ -102,9 +147,16 @@ def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], la
         raise ValueError(f"Expected K/V shape {shape}; got key={tuple(key.shape)}, value={tuple(value.shape)}")
     if key.dtype != kv.dtype or value.dtype != kv.dtype:
         raise ValueError(f"K/V tensors must have dtype {kv.dtype}")
-    slots = np.fromiter((cache.slot_of(r, p) if hasattr(cache, "slot_of") else _slot(cache, r, p)
-                         for r, p in zip(request_ids, positions)), dtype=np.int64, count=len(request_ids))
-    slot_t = torch.from_numpy(slots).to(key.device, non_blocking=True)
+
+    def build():
+        slots = np.fromiter((cache.slot_of(r, p) if hasattr(cache, "slot_of") else _slot(cache, r, p)
+                             for r, p in zip(request_ids, positions)), dtype=np.int64, count=len(request_ids))
+        host = torch.from_numpy(slots)
+        if key.device.type == "cuda":
+            host = host.pin_memory()
+        return host.to(key.device, non_blocking=True)
+
+    slot_t = _memo(cache, "slots", request_ids, positions, key.device, build)
     ops.reshape_and_cache(key, value, kv.k_cache, kv.v_cache, slot_t, layer)
 
 

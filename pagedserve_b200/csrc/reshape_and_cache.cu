@@ -25,8 +25,11 @@ __global__ void __launch_bounds__(256) reshape_and_cache_kernel(
     int64_t vsh, char* __restrict__ k_cache, char* __restrict__ v_cache, const int64_t* __restrict__ slots,
     int32_t num_tokens, int64_t layer_base_tiles, int32_t hkv, int32_t block_size, int32_t row_bytes,
     int64_t pool_slots, int32_t* err) {
-  // a decode launched right after may start its prologue now (it waits for
-  // this grid before reading the pool)
+  // Launched as a programmatic dependent: wait for the stream predecessor
+  // (which may produce key, value or the slots, or read the pool) before
+  // touching anything, and only then let a decode launched right after start
+  // its prologue (it waits for this grid before reading the pool).
+  pdl_wait();
   pdl_launch_dependents();
   const int nvec = row_bytes / static_cast<int>(sizeof(V));
   const int64_t per_token = static_cast<int64_t>(hkv) * nvec;
@@ -85,21 +88,23 @@ extern "C" int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int6
   const char* vp = static_cast<const char*>(value);
   char* kc = static_cast<char*>(k_cache);
   char* vc = static_cast<char*>(v_cache);
+  cudaError_t e = cudaSuccess;
   if (vec16) {
     discard_stale_error();
-    reshape_and_cache_kernel<uint4><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
-        row_bytes, pool_slots, error_flag);
+    e = launch_pdl(reshape_and_cache_kernel<uint4>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
+                   ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
+                   row_bytes, pool_slots, error_flag);
   } else if (esz == 4) {
     discard_stale_error();
-    reshape_and_cache_kernel<uint32_t><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
-        row_bytes, pool_slots, error_flag);
+    e = launch_pdl(reshape_and_cache_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
+                   ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
+                   row_bytes, pool_slots, error_flag);
   } else {
     discard_stale_error();
-    reshape_and_cache_kernel<uint16_t><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        kp, kst, ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
-        row_bytes, pool_slots, error_flag);
+    e = launch_pdl(reshape_and_cache_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
+                   ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
+                   row_bytes, pool_slots, error_flag);
   }
+  if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }

@@ -99,6 +99,7 @@ class BlockTable:
 
     def __init__(self) -> None:
         self._blocks: list[int] = []
+        self._owner: "PagedKVCache | None" = None  # told of every change (metadata epoch)
 
     @property
     def num_blocks(self) -> int:
@@ -108,6 +109,8 @@ class BlockTable:
         if physical_block_id < 0:
             raise ValueError("physical_block_id cannot be negative")
         self._blocks.append(physical_block_id)
+        if self._owner is not None:
+            self._owner._epoch += 1
 
     def get_physical_block(self, logical_block_id: int) -> int:
         if not 0 <= logical_block_id < len(self._blocks):
@@ -119,6 +122,8 @@ class BlockTable:
 
     def clear(self) -> None:
         self._blocks.clear()
+        if self._owner is not None:
+            self._owner._epoch += 1
 
 
 class KVCache:
@@ -190,6 +195,7 @@ class PagedKVCache:
                                 head_dim=head_dim, block_size=block_size, dtype=dtype, device=device)
         self._tables: dict[str, BlockTable] = {}
         self._counts: dict[str, int] = {}
+        self._epoch = 0
 
     # -- allocation ---------------------------------------------------------
     def allocate(self, request_id: str, num_tokens: int) -> None:
@@ -200,8 +206,10 @@ class PagedKVCache:
         table = BlockTable()
         for blk in self.block_manager.allocate(request_id=request_id, num_tokens=num_tokens):
             table.append(blk)
+        table._owner = self
         self._tables[request_id] = table
         self._counts[request_id] = num_tokens
+        self._epoch += 1
 
     def append_tokens(self, request_id: str, num_tokens: int) -> None:
         """Grow a request's capacity; new blocks only when a block boundary is crossed."""
@@ -216,12 +224,14 @@ class PagedKVCache:
             for blk in self.block_manager.allocate_blocks(request_id=request_id, num_blocks=extra):
                 self._tables[request_id].append(blk)
         self._counts[request_id] = old + num_tokens
+        self._epoch += 1
 
     def free(self, request_id: str) -> None:
         self._validate_request(request_id)
-        del self._tables[request_id]
+        self._tables.pop(request_id)._owner = None
         del self._counts[request_id]
         self.block_manager.free(request_id)
+        self._epoch += 1
 
     # -- queries ---------------------------------------------------------------
     def get_block_table(self, request_id: str) -> BlockTable:
@@ -231,6 +241,13 @@ class PagedKVCache:
     def token_count(self, request_id: str) -> int:
         self._validate_request(request_id)
         return self._counts[request_id]
+
+    @property
+    def metadata_epoch(self) -> int:
+        """Changes whenever a request's blocks or token count change; the
+        batched path reuses device copies of block tables built at the same
+        epoch for the same requests and positions."""
+        return self._epoch
 
     @property
     def free_blocks(self) -> int:

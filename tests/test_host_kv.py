@@ -200,3 +200,73 @@ def test_batched_helpers():
     assert c.slot_of("a", 16) == 3 * 16 and c.slot_of("c", 64) == 8 * 16
     with pytest.raises(IndexError):
         c.slot_of("a", 17)
+
+
+def test_metadata_epoch_tracks_every_change():
+    c = PagedKVCache(num_blocks=16, num_layers=1, num_kv_heads=2, head_dim=8, block_size=4, dtype=torch.float32,
+                     device="cpu")
+    seen = [c.metadata_epoch]
+
+    def changed():
+        seen.append(c.metadata_epoch)
+        return seen[-1] != seen[-2]
+
+    c.allocate("a", 3)
+    assert changed()
+    c.append_tokens("a", 1)      # same block, more tokens: positions valid now differ
+    assert changed()
+    c.append_tokens("a", 0)      # no change
+    assert not changed()
+    c.get_block_table("a").append(9)  # direct table edit by a caller
+    assert changed()
+    c.token_count("a")
+    assert not changed()
+    c.free("a")
+    assert changed()
+
+
+def test_host_metadata_reused_within_an_epoch():
+    from pagedserve_b200 import attention
+    c = PagedKVCache(num_blocks=32, num_layers=2, num_kv_heads=2, head_dim=8, block_size=4, dtype=torch.float32,
+                     device="cpu")
+    for rid, n in (("x", 5), ("y", 9)):
+        c.allocate(rid, n)
+    dev = torch.device("cpu")
+    t1, l1, w1 = attention._host_metadata(c, ["x", "y"], [4, 8], dev)
+    t2, l2, w2 = attention._host_metadata(c, ["x", "y"], [4, 8], dev)
+    assert t1 is t2 and l1 is l2 and w1 == w2 == 3
+    assert l1.tolist() == [5, 9]
+    assert t1.tolist() == [c.get_block_table("x").get_blocks() + [0], c.get_block_table("y").get_blocks()]
+    t3, l3, _ = attention._host_metadata(c, ["x", "y"], [3, 8], dev)   # other positions
+    assert t3 is not t1 and l3.tolist() == [4, 9]
+    c.append_tokens("x", 4)                                             # new epoch
+    t4, l4, w4 = attention._host_metadata(c, ["x", "y"], [8, 8], dev)
+    assert w4 == 3 and l4.tolist() == [9, 9] and t4.tolist()[0] == c.get_block_table("x").get_blocks()
+    with pytest.raises(ValueError, match="Invalid position"):
+        attention._host_metadata(c, ["x", "y"], [9, 8], dev)
+    attention.clear_metadata_cache(c)
+    assert len(c._psb_metadata) == 0
+
+
+def test_host_metadata_without_epoch_rebuilds():
+    """A cache object without ``metadata_epoch`` (the reference's) is rebuilt every call."""
+    from pagedserve_b200 import attention
+    inner = PagedKVCache(num_blocks=8, num_layers=1, num_kv_heads=1, head_dim=8, block_size=4, dtype=torch.float32,
+                         device="cpu")
+    inner.allocate("r", 6)
+
+    class Plain:
+        block_size = 4
+        kv_cache = inner.kv_cache
+
+        def token_count(self, rid):
+            return inner.token_count(rid)
+
+        def get_block_table(self, rid):
+            return inner.get_block_table(rid)
+
+    plain = Plain()
+    a = attention._host_metadata(plain, ["r"], [5], torch.device("cpu"))
+    b = attention._host_metadata(plain, ["r"], [5], torch.device("cpu"))
+    assert a[0] is not b[0] and torch.equal(a[0], b[0])
+    assert not hasattr(plain, "_psb_metadata")
