@@ -71,7 +71,9 @@ int psb_last_cuda_error(void);
  *     k_cache[layer, block, h, offset, :] = key[t, h, :]   (and v likewise)
  * bit-exactly.  A negative slot writes nothing (padding row).  key/value are
  * [num_tokens, num_kv_heads, head_dim] with element strides (stride_t,
- * stride_h) and unit stride along head_dim.
+ * stride_h) and unit stride along head_dim.  Launched as a programmatic
+ * dependent: it may start before its stream predecessor ends (it waits for
+ * it before touching memory) and lets the kernel after it start at once.
  */
 int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int64_t key_stride_h, const void* value,
                           int64_t value_stride_t, int64_t value_stride_h, void* k_cache, void* v_cache,
@@ -116,9 +118,11 @@ int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int
  * sequences that span several warps in a second kernel on the same stream;
  * other geometries run a CUDA-core kernel.  Context lengths and block tables
  * are read before the kernel waits on its stream predecessor (programmatic
- * dependent launch): they must not be written by the kernel launched
- * immediately before this call.  Calls sharing one workspace must not overlap
- * on the GPU.
+ * dependent launch), possibly while the kernels this library launched just
+ * before (reshape_and_cache, decode, combine, varlen_prefill) still run:
+ * they must be written by an earlier kernel that is not one of those (an
+ * ordinary launch such as pack_step's, or a host copy).  Calls sharing one
+ * workspace must not overlap on the GPU.
  */
 int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out, int64_t o_stride_b,
                      int64_t o_stride_h, const void* k_cache, const void* v_cache, const int32_t* block_tables,

@@ -15,8 +15,17 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // SM count of the current device (cached per device).
 int device_sm_count();
 
+// Ask for the largest shared-memory carve-out for ``func`` (once per device).
+// Every kernel of this library does, so a decode CTA (188 KB of shared
+// memory) can start on an SM where a small kernel of the same stream - the
+// split-K combine, reshape_and_cache - still runs: an SM changes its L1 /
+// shared split only when idle, so differing preferences would serialise
+// them.
+bool prefer_max_shared(const void* func);
+
 // Max resident CTAs per SM for ``func`` at ``threads`` and ``smem`` dynamic
-// bytes; raises the kernel's dynamic shared-memory limit when needed.
+// bytes; raises the kernel's dynamic shared-memory limit when needed (and
+// sets the carve-out preference above).
 bool kernel_occupancy(const void* func, int threads, size_t smem, int* blocks_per_sm);
 
 // Remember a CUDA error for psb_last_cuda_error(); returns PSB_ERR_CUDA.

@@ -51,7 +51,6 @@ struct DecodeParams {
   float* part_o;     // [max_units, group, head_dim]
   float* part_ml;    // [max_units, group, 2]
   int32_t* counters; // [batch * hkv]
-  int32_t* plan;     // [batch + 1]: block prefix over sequences (fast path)
   int32_t total_warps;  // warps of the fast-path decode grid
   int64_t max_units;
   int32_t* err;
@@ -294,6 +293,7 @@ constexpr int kFastWarps = 6;
 constexpr int kFastThreads = kFastWarps * 32;
 constexpr int kRing = 3;              // slots per warp
 constexpr int kFastMinBlocks = 8;     // blocks per warp below which the grid shrinks
+constexpr int kMaxFastCtas = 160;     // grid limit (one CTA per SM; B200 has 148)
 
 constexpr int kPartFloats = 16 * 64;  // one partial: 16 tile rows x 64 dims
 constexpr int kMaxFastBatch = 1 << 20;
@@ -312,8 +312,7 @@ struct FastGeom {
 __device__ __forceinline__ int blocks_of(int ctx) { return ctx <= 0 ? 1 : (ctx + 15) >> 4; }
 
 // s_ctx[b] = clamped context; bpre[b] = exclusive prefix of blocks_of over
-// sequences, bpre[B] = Nb.  Every CTA computes the same arrays; CTA 0 also
-// leaves bpre in the workspace for the combine kernel.
+// sequences, bpre[B] = Nb.  Every CTA computes the same arrays.
 __device__ int build_block_prefix(const DecodeParams& p, int32_t* bpre, int32_t* s_ctx) {
   __shared__ int32_t warp_sums[kFastWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -344,8 +343,6 @@ __device__ int build_block_prefix(const DecodeParams& p, int32_t* bpre, int32_t*
   for (int w = 0; w < kFastWarps; ++w) total += warp_sums[w];
   if (tid == 0) bpre[B] = total;
   __syncthreads();
-  if (blockIdx.x == 0)
-    for (int i = tid; i <= B; i += kFastThreads) p.plan[i] = bpre[i];
   return total;
 }
 
@@ -755,50 +752,82 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
 }
 
 // ---------------------------------------------------------------------------
-// split-K merge for the fast path: one CTA per (sequence, head group).  The
-// warps whose ranges meet the sequence follow from the block prefix the
-// decode launch left in the workspace; a sequence inside one warp's range
-// was finished there and the CTA exits.  Otherwise thread (row, 4-dim slice)
-// loads the partials of up to kCombBatch warps at once - one memory round
-// trip for most sequences - rescales them to their common maximum and writes
-// the normalised output.  Launched right after decode_fast_kernel on the same
-// stream; griddepcontrol.wait makes every partial visible.
+// split-K merge for the fast path: one CTA per (sequence, head group).
+// Launched right after decode_fast_kernel on the same stream, it starts while
+// the decode still runs: from the context lengths alone (stable for the whole
+// decode) it works out which warps hold pieces of its sequence, exactly as
+// the decode split them, and lists their partial slots in shared memory.  A
+// sequence inside one warp's range was finished by the decode and the CTA
+// exits.  Then griddepcontrol.wait - every partial visible - and thread (row,
+// 4-dim slice) loads the partials of up to kCombBatch warps at once (one
+// memory round trip for most sequences), rescales them to their common
+// maximum and writes the normalised output.
 // ---------------------------------------------------------------------------
 constexpr int kCombThreads = 256;  // 16 tile rows x 16 slices of 4 dims
 constexpr int kCombBatch = 12;
 
 template <typename T, int HP>
 __global__ void __launch_bounds__(kCombThreads, 2) decode_combine_kernel(const DecodeParams p) {
+  __shared__ int32_t s_slot[kFastWarps * kMaxFastCtas];  // a piece per warp at most
+  __shared__ int32_t s_red[2][kCombThreads / 32];
+  __shared__ int32_t s_nblk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int groups = p.hkv / HP;
+  const int b = blockIdx.x / groups, hg = blockIdx.x - b * groups;
+  // blocks before sequence b and in total (item counts are below 2^31), with
+  // the decode's clamp of each length (the decode flags bad lengths)
+  int before = 0, total = 0;
+  for (int i = tid; i < p.batch; i += kCombThreads) {
+    int n = p.ctx[i];
+    n = n < 0 ? 0 : (n > p.max_context ? p.max_context : n);
+    const int nb = blocks_of(n);
+    total += nb;
+    before += i < b ? nb : 0;
+    if (i == b) s_nblk = nb;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    before += __shfl_xor_sync(0xffffffffu, before, o);
+    total += __shfl_xor_sync(0xffffffffu, total, o);
+  }
+  if (lane == 0) {
+    s_red[0][warp] = before;
+    s_red[1][warp] = total;
+  }
+  __syncthreads();
+  before = total = 0;
+#pragma unroll
+  for (int w = 0; w < kCombThreads / 32; ++w) {
+    before += s_red[0][w];
+    total += s_red[1][w];
+  }
+  const int64_t nb_total = total;
+  const Split split(nb_total * groups, p.total_warps);
+  const int64_t first = hg * nb_total + before, last = first + s_nblk - 1;
+  const int wa = split.warp_of(first), wb = split.warp_of(last);
+  if (wa == wb) return;  // inside one warp's range: written by the decode
+  const int np = wb - wa + 1;
+  for (int k = tid; k < np; k += kCombThreads) {
+    const int64_t s0 = split.start(wa + k), s1 = split.start(wa + k + 1);
+    s_slot[k] = s0 == s1 ? -1 : 2 * (wa + k) + (s0 < first ? 1 : 0);  // an empty range wrote nothing
+  }
+  __syncthreads();
+
   pdl_wait();
   // the next kernel on the stream may launch now; if it is a programmatic
   // dependent it waits for this grid before touching memory
   pdl_launch_dependents();
-  const int groups = p.hkv / HP;
-  const int b = blockIdx.x / groups, hg = blockIdx.x - (blockIdx.x / groups) * groups;
-  const int32_t* bpre = p.plan;
-  const int64_t nb_total = bpre[p.batch];
-  const int64_t n_items = nb_total * groups;
-  const Split split(n_items, p.total_warps);
-  const int64_t first = hg * nb_total + bpre[b], last = hg * nb_total + bpre[b + 1] - 1;
-  const int wa = split.warp_of(first), wb = split.warp_of(last);
-  if (wa == wb) return;  // inside one warp's range: written by the decode
-  const int tid = threadIdx.x, r = tid >> 4, q4 = tid & 15;
-  const int first32 = static_cast<int>(first);  // item counts are below 2^31
-  const int w_last = wb;
+  const int r = tid >> 4, q4 = tid & 15;
   float M = -INFINITY, L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int w0 = wa; w0 <= w_last; w0 += kCombBatch) {
+  for (int k0 = 0; k0 < np; k0 += kCombBatch) {
     float2 ml[kCombBatch];
     float4 v[kCombBatch];
-    int st = static_cast<int>(split.start(w0));
 #pragma unroll
     for (int k = 0; k < kCombBatch; ++k) {
       ml[k] = make_float2(-INFINITY, 0.f);
       v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const int s0 = st;
-      const int nx = w0 + k <= w_last ? static_cast<int>(split.start(w0 + k + 1)) : s0;
-      st = nx;
-      if (w0 + k <= w_last && s0 != nx) {  // an empty range wrote nothing
-        const int slot_id = 2 * (w0 + k) + (s0 < first32 ? 1 : 0);
+      const int slot_id = k0 + k < np ? s_slot[k0 + k] : -1;
+      if (slot_id >= 0) {
         ml[k] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + slot_id * 16 + r);
         v[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o) + slot_id * (kPartFloats / 4) + r * 16 + q4);
       }
@@ -1011,21 +1040,17 @@ WorkspaceLayout workspace_layout(const SplitGeom& sg, int head_dim) {
   return w;
 }
 
-// Fast path: [block prefix: batch + 1 int32 | pad to 256][partial max/sum:
-// slots * 16 * 2 f32][partial outputs: slots * 16 * 64 f32], two partial
-// slots per warp of a grid of at most kMaxFastCtas CTAs (one per SM; B200 has
-// 148).  Nothing needs initialising.
-constexpr int kMaxFastCtas = 160;
-
+// Fast path: [partial max/sum: slots * 16 * 2 f32][partial outputs: slots *
+// 16 * 64 f32], two partial slots per warp of a grid of at most kMaxFastCtas
+// CTAs.  The size does not depend on the batch; nothing needs initialising.
 struct FastLayout {
-  size_t plan_off, ml_off, o_off, total;
+  size_t ml_off, o_off, total;
 };
 
-FastLayout fast_layout(int batch) {
+FastLayout fast_layout() {
   FastLayout f;
   const size_t slots = 2 * static_cast<size_t>(kFastWarps) * kMaxFastCtas;
-  f.plan_off = 0;
-  f.ml_off = align_up(sizeof(int32_t) * (static_cast<size_t>(batch) + 1), 256);
+  f.ml_off = 0;
   f.o_off = align_up(f.ml_off + sizeof(float) * slots * 32, 256);
   f.total = f.o_off + sizeof(float) * slots * kPartFloats;
   return f;
@@ -1050,6 +1075,7 @@ int launch_fast(DecodeParams prm, cudaStream_t stream, int max_ctas) {
                              stream, prm);
   if (e != cudaSuccess) return record_cuda_error(e);
   const int64_t merges = static_cast<int64_t>(prm.batch) * (prm.hkv / HP);
+  if (!prefer_max_shared(reinterpret_cast<const void*>(decode_combine_kernel<T, HP>))) return PSB_ERR_CUDA;
   e = launch_pdl(decode_combine_kernel<T, HP>, dim3(static_cast<unsigned>(merges)), dim3(kCombThreads), 0, stream,
                  prm);
   if (e != cudaSuccess) return record_cuda_error(e);
@@ -1102,7 +1128,7 @@ extern "C" size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads
   // sized for whichever path the geometry allows; large enough for the other
   // (the fast path also depends on pointer alignment, known only at the call)
   const int hp = fast_heads_per_unit(dtype, head_dim, block_size, group, num_kv_heads);
-  const size_t fast = hp ? fast_layout(batch).total : 0;
+  const size_t fast = hp ? fast_layout().total : 0;
   const size_t gen = workspace_layout(split_geometry(batch, num_kv_heads, group, max_context), head_dim).total;
   return std::max(fast, gen);
 }
@@ -1170,12 +1196,11 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   char* ws = static_cast<char*>(workspace);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (hp) {
-    const FastLayout fl = fast_layout(batch);
+    const FastLayout fl = fast_layout();
     const int max_ctas = std::min(sms, kMaxFastCtas);
     if (workspace_bytes < fl.total) return PSB_ERR_WORKSPACE;
     p.chunk = 0;
     p.counters = nullptr;
-    p.plan = reinterpret_cast<int32_t*>(ws + fl.plan_off);
     p.part_ml = reinterpret_cast<float*>(ws + fl.ml_off);
     p.part_o = reinterpret_cast<float*>(ws + fl.o_off);
     p.max_units = 0;
@@ -1188,7 +1213,6 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   if (workspace_bytes < wl.total) return PSB_ERR_WORKSPACE;
   p.chunk = sg.chunk;
   p.counters = reinterpret_cast<int32_t*>(ws + wl.counters_off);
-  p.plan = nullptr;
   p.part_ml = reinterpret_cast<float*>(ws + wl.ml_off);
   p.part_o = reinterpret_cast<float*>(ws + wl.o_off);
   p.max_units = sg.max_units;

@@ -25,12 +25,13 @@ __global__ void __launch_bounds__(256) reshape_and_cache_kernel(
     int64_t vsh, char* __restrict__ k_cache, char* __restrict__ v_cache, const int64_t* __restrict__ slots,
     int32_t num_tokens, int64_t layer_base_tiles, int32_t hkv, int32_t block_size, int32_t row_bytes,
     int64_t pool_slots, int32_t* err) {
-  // Launched as a programmatic dependent: wait for the stream predecessor
-  // (which may produce key, value or the slots, or read the pool) before
-  // touching anything, and only then let a decode launched right after start
-  // its prologue (it waits for this grid before reading the pool).
-  pdl_wait();
+  // A decode launched right after may start now: its prologue reads only
+  // lengths and block tables, and it waits for this grid before reading the
+  // pool.  This grid itself is a programmatic dependent: it waits for its
+  // stream predecessor (which may produce key, value or the slots, or read
+  // the pool) before touching anything.
   pdl_launch_dependents();
+  pdl_wait();
   const int nvec = row_bytes / static_cast<int>(sizeof(V));
   const int64_t per_token = static_cast<int64_t>(hkv) * nvec;
   const int64_t total = per_token * num_tokens;
@@ -91,16 +92,19 @@ extern "C" int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int6
   cudaError_t e = cudaSuccess;
   if (vec16) {
     discard_stale_error();
+    if (!prefer_max_shared(reinterpret_cast<const void*>(reshape_and_cache_kernel<uint4>))) return PSB_ERR_CUDA;
     e = launch_pdl(reshape_and_cache_kernel<uint4>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
                    ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
                    row_bytes, pool_slots, error_flag);
   } else if (esz == 4) {
     discard_stale_error();
+    if (!prefer_max_shared(reinterpret_cast<const void*>(reshape_and_cache_kernel<uint32_t>))) return PSB_ERR_CUDA;
     e = launch_pdl(reshape_and_cache_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
                    ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
                    row_bytes, pool_slots, error_flag);
   } else {
     discard_stale_error();
+    if (!prefer_max_shared(reinterpret_cast<const void*>(reshape_and_cache_kernel<uint16_t>))) return PSB_ERR_CUDA;
     e = launch_pdl(reshape_and_cache_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, kp, kst,
                    ksh, vp, vst, vsh, kc, vc, slot_mapping, num_tokens, layer_base_tiles, num_kv_heads, block_size,
                    row_bytes, pool_slots, error_flag);
