@@ -5,8 +5,10 @@ Workload (one "step" = one layer call of the decode hot path over one batch):
 256 sequences, context lengths lognormal(median 1024, sigma 0.8) clipped to
 [16, 8192]; Qwen2.5-0.5B attention geometry (14 q heads, 2 kv heads, head_dim
 64), block_size 16, bf16; physical blocks shuffled across a pool of 1.25x
-the need; the step writes one new token per sequence through a slot mapping
-(reshape_and_cache) and runs split-K paged decode attention over the pool.
+the need; the step writes one new token per sequence into the pool and runs
+split-K paged decode attention over it - one fused launch that stores each
+row's token at its last position through the block table (the slot the
+reshape_and_cache slot mapping names) - plus the split-K combine.
 Synthetic seeded data (no dataset or weights are involved).  The pool holds
 the model's 24 layers and consecutive steps are consecutive layers, so every
 step streams ~180 MB of KV that is not resident in the 126 MB L2.  Steps run
@@ -371,7 +373,7 @@ def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | No
 
 
 def run_b200(args, world, rank, local):
-    from pagedserve_b200 import ops, paged_decode_attention, write_tokens
+    from pagedserve_b200 import ops, paged_decode_attention_with_write
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     pg = None
@@ -387,52 +389,56 @@ def run_b200(args, world, rank, local):
     out = torch.empty_like(w["q"])
     err = torch.zeros(1, dtype=torch.int32, device=device)
 
-    def reshape(layer):
-        ops.reshape_and_cache(w["new_k"], w["new_v"], k, v, w["slots"], layer, error_flag=err)
+    def step(layer):  # the decode step: new token stored + attention, one launch (and the combine)
+        ops.paged_decode(w["q"], k, v, w["tables"], w["lens_t"], layer, out=out, error_flag=err,
+                         new_key=w["new_k"], new_value=w["new_v"])
 
-    def decode(layer):
+    def two_launch(layer):  # the same step as reshape_and_cache, then decode
+        ops.reshape_and_cache(w["new_k"], w["new_v"], k, v, w["slots"], layer, error_flag=err)
+        ops.paged_decode(w["q"], k, v, w["tables"], w["lens_t"], layer, out=out, error_flag=err)
+
+    def decode_only(layer):
         ops.paged_decode(w["q"], k, v, w["tables"], w["lens_t"], layer, out=out, error_flag=err)
 
     for layer in range(LAYERS):  # warm the library, size the workspace
-        reshape(layer)
-        decode(layer)
+        step(layer)
+        two_launch(layer)
     torch.cuda.synchronize()
 
-    # One CUDA graph per decode iteration: the 24 layers' attention calls in
-    # order, each reshape_and_cache then decode + split-K combine, chained by
-    # programmatic dependent launch.  A step is one layer call: K steps are
-    # K // 24 iteration graphs plus one graph of the first K % 24 layers.
-    # Decode-only graphs of the same shape time the kernel for the roofline,
-    # and one graph per layer call shows the cost of launching each alone.
+    # One CUDA graph per decode iteration: the 24 layers' decode steps in
+    # order, each chained to the one before by programmatic dependent launch.
+    # A step is one layer call: K steps are K // 24 iteration graphs plus one
+    # graph of the first K % 24 layers.  Graphs of the same shape time the
+    # decode kernel alone (for the roofline) and the two-launch form of the
+    # step, and one graph per layer call shows the cost of launching each
+    # alone.
     stream = torch.cuda.Stream(device)
 
-    def capture(layers, with_reshape=True):
+    def capture(fn, layers):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for layer in layers:
-                if with_reshape:
-                    reshape(layer)
-                decode(layer)
+                fn(layer)
         return g
 
     full, rem = divmod(args.steps, LAYERS)
+    graphs = {}
     with torch.cuda.stream(stream):
-        g_iter = capture(range(LAYERS))
-        g_rem = capture(range(rem)) if rem else None
-        g_dec_iter = capture(range(LAYERS), with_reshape=False)
-        g_dec_rem = capture(range(rem), with_reshape=False) if rem else None
-        g_single = [capture([layer]) for layer in range(LAYERS)]
+        for name, fn in (("step", step), ("decode", decode_only), ("two", two_launch)):
+            graphs[name] = (capture(fn, range(LAYERS)), capture(fn, range(rem)) if rem else None)
+        g_single = [capture(step, [layer]) for layer in range(LAYERS)]
     torch.cuda.synchronize()
 
-    def run_steps(g_all, g_part):
+    def run_steps(name):
+        g_all, g_part = graphs[name]
         for _ in range(full):
             g_all.replay()
         if g_part is not None:
             g_part.replay()
 
     for _ in range(-(-args.warmup // LAYERS)):  # at least W warm-up layer calls of each kind
-        g_iter.replay()
-        g_dec_iter.replay()
+        for g_all, _ in graphs.values():
+            g_all.replay()
     for g in g_single:
         g.replay()
     torch.cuda.synchronize()
@@ -457,10 +463,11 @@ def run_b200(args, world, rank, local):
     clocks = Clocks(gpu_ids if rank == 0 else [])
     if rank == 0:
         clocks.__enter__()
-    step_ms = timed(lambda: run_steps(g_iter, g_rem)) / args.steps
+    step_ms = timed(lambda: run_steps("step")) / args.steps
     # the decode kernel alone (decode + split-K combine), same K layer calls
-    dec_ms = timed(lambda: run_steps(g_dec_iter, g_dec_rem)) / args.steps
-    # the same layer calls, one graph launch each
+    dec_ms = timed(lambda: run_steps("decode")) / args.steps
+    # the step as two launches (reshape_and_cache, decode), and one graph launch per layer call
+    two_ms = timed(lambda: run_steps("two")) / args.steps
     single_ms = timed(lambda: [g_single[s % LAYERS].replay() for s in range(args.steps)]) / args.steps
     if rank == 0:
         clocks.__exit__(None, None, None)
@@ -478,13 +485,12 @@ def run_b200(args, world, rank, local):
 
     def e2e_step(s):
         layer = s % LAYERS
-        if layer == 0:  # a new decode iteration: block tables and slots are rebuilt and copied once
+        if layer == 0:  # a new decode iteration: block tables are rebuilt and copied once
             clear_metadata_cache(cache)
         qd = q_host.to(device, non_blocking=True).unsqueeze(2)  # [B, Hq, 1, D]
         kd = k_host.to(device, non_blocking=True)
         vd = v_host.to(device, non_blocking=True)
-        write_tokens(cache, ids, positions, layer, kd, vd)
-        o = paged_decode_attention(qd, cache, ids, positions, layer)
+        o = paged_decode_attention_with_write(qd, kd, vd, cache, ids, positions, layer)
         o_host.copy_(o, non_blocking=True)
 
     for s in range(min(args.warmup, 3)):
@@ -502,7 +508,7 @@ def run_b200(args, world, rank, local):
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     width = cache.table_rows(ids).shape[1]
     iterations = -(-args.steps // LAYERS)  # metadata copies inside the timed region
-    meta_bytes = 8 * batch + 4 * batch * (width + 1)  # slots; table + lengths
+    meta_bytes = 4 * batch * (width + 1)  # table + lengths
     h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + meta_bytes * iterations / args.steps
     d2h = o_host.numel() * 2
 
@@ -514,10 +520,11 @@ def run_b200(args, world, rank, local):
     lens = w["lens"]
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
     rank_dec_ms = dec_ms
-    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms},
-                               device, op="max")
+    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
+                                "two_ms": two_ms}, device, op="max")
     work = aggregate_counters({"bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())}, device, op="sum")
     step_ms, dec_ms, e2e_ms, single_ms = times["step_ms"], times["dec_ms"], times["e2e_ms"], times["single_ms"]
+    two_ms = times["two_ms"]
     total_bytes, total_seqs = work["bytes"], int(work["seqs"])
     value = total_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
@@ -538,11 +545,13 @@ def run_b200(args, world, rank, local):
                        "rank0_sequences": batch, "rank0_sum_ctx": int(lens.sum()),
                        "l2": "inputs larger than L2: a 24-layer pool, consecutive steps are consecutive "
                              "layers (~180 MB of KV each, read with an evict-first L2 policy)",
-                       "launch": "one CUDA graph per decode iteration: 24 layer calls, each reshape_and_cache "
-                                 "then decode + split-K combine, chained by programmatic dependent launch; a "
-                                 "step is one layer call",
+                       "launch": "one CUDA graph per decode iteration: 24 layer calls, each the fused decode "
+                                 "step (new token stored through the block table + split-K attention, then the "
+                                 "combine), chained by programmatic dependent launch; a step is one layer call",
                        "per_layer_graph_ms": round(single_ms, 5),
                        "per_layer_graph_note": "the same layer calls launched as one CUDA graph each",
+                       "two_launch_ms": round(two_ms, 5),
+                       "two_launch_note": "the step as reshape_and_cache (slot mapping) then decode, same graphs",
                        "parallelism": f"sequence-sharded x{world}"},
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
@@ -559,18 +568,19 @@ def run_b200(args, world, rank, local):
                                            "(decode ncu summary under profiles/)"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
-                    "path": "per layer call: q, new k, new v copied from pinned host buffers, write_tokens + "
-                            "paged_decode_attention (reference-facing API), output copied back; block tables "
-                            "and slots built and copied once per 24-layer iteration"},
-            "gpu_launches": 3 * args.steps,
-            "gpu_launches_note": "per step: reshape_and_cache, decode, combine",
+                    "path": "per layer call: q, new k, new v copied from pinned host buffers, "
+                            "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
+                            "one launch), output copied back; block tables built and copied once per 24-layer "
+                            "iteration"},
+            "gpu_launches": 2 * args.steps,
+            "gpu_launches_note": "per step: decode (with the new-token store), combine",
             "clocks": clocks.summary(),
             "prefill": prefill,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    for g in [g_iter, g_rem, g_dec_iter, g_dec_rem] + g_single:
+    for g in [g for pair in graphs.values() for g in pair] + g_single:
         if g is not None:
             g.reset()
     if pg is not None:

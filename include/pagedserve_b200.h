@@ -132,6 +132,31 @@ int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, 
                      void* workspace, size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream);
 
 /*
+ * paged_decode_append: the decode step's cache write and attention in one
+ * launch.  Equivalent to writing row b's new key/value
+ * ([batch, num_kv_heads, head_dim], element strides (stride_b, stride_h),
+ * unit stride along head_dim) at position context_lens[b] - 1 of sequence
+ * b - located through block_tables as PagedKVCache.write_token does
+ * (pagedserve/engine/paged_kv_cache.py:187-200), the per-row loop of
+ * pagedserve/attention/batched_paged_attention.py:115-124 - followed by
+ * psb_paged_decode over the first context_lens[b] tokens, which include it.
+ * The pool bytes written and the outputs are identical to that sequence.
+ * Rows with context_lens[b] == 0 write nothing.  Each row's last block must
+ * belong to that row alone (no two rows share it), as with any decode step.
+ * Arguments, workspace, results and error behaviour are otherwise
+ * psb_paged_decode's.
+ */
+int psb_paged_decode_append(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
+                            int64_t o_stride_b, int64_t o_stride_h, void* k_cache, void* v_cache,
+                            const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
+                            const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
+                            const int32_t* block_tables, int64_t table_stride, const int32_t* context_lens,
+                            int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers, int64_t num_blocks,
+                            int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype,
+                            int32_t max_context, float scale, void* workspace, size_t workspace_bytes,
+                            int32_t* error_flag, psb_stream_t stream);
+
+/*
  * paged_decode_static: psb_paged_decode without a caller workspace.  It has
  * no counterpart in the reference (whose Triton decode needs no scratch); it
  * exists for callers that cannot allocate device memory where they launch

@@ -5,6 +5,7 @@ Public surface:
 * ``paged_decode_attention`` - drop-in for ``triton_paged_decode_attention``
   (pagedserve/attention/triton_paged_decode.py:98)
 * ``write_tokens`` - batched replacement of the per-row ``write_token`` loop
+* ``paged_decode_attention_with_write`` - both in one launch
 * ``ops.reshape_and_cache / paged_decode / varlen_prefill / pack_step`` -
   tensor-level API over the C ABI (include/pagedserve_b200.h)
 * ``PagedKVCache`` and friends - host-side block bookkeeping with the
@@ -14,10 +15,10 @@ Public surface:
 """
 
 from . import ops
-from .attention import paged_decode_attention, write_tokens
+from .attention import paged_decode_attention, paged_decode_attention_with_write, write_tokens
 from .paged_kv import BlockManager, BlockTable, KVCache, PagedKVCache
 from .sharding import SequenceDispatcher
 
-__all__ = ["ops", "paged_decode_attention", "write_tokens", "BlockManager", "BlockTable", "KVCache",
-           "PagedKVCache", "SequenceDispatcher"]
+__all__ = ["ops", "paged_decode_attention", "paged_decode_attention_with_write", "write_tokens", "BlockManager",
+           "BlockTable", "KVCache", "PagedKVCache", "SequenceDispatcher"]
 __version__ = "0.1.0"

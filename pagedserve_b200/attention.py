@@ -101,6 +101,15 @@ def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str
 
     Drop-in for ``triton_paged_decode_attention`` (triton_paged_decode.py:98-104).
     """
+    tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
+    kv = cache.kv_cache
+    return ops.paged_decode(query, kv.k_cache, kv.v_cache, tables, lengths, layer,
+                            max_context=width * cache.block_size)
+
+
+def _validated_metadata(query, cache, request_ids, positions, layer):
+    """The reference wrapper's checks, in its order and with its messages
+    (triton_paged_decode.py:106-141), then the device table and lengths."""
     if not query.is_cuda:
         raise ValueError("B200 paged attention requires CUDA")
     if query.ndim != 4 or query.shape[2] != 1:
@@ -127,8 +136,37 @@ def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str
     if not 0 <= layer < kv.k_cache.shape[0]:
         raise ValueError("Invalid layer")
     tables, lengths, width = _host_metadata(cache, request_ids, positions, query.device)
+    return tables, lengths, width
+
+
+def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, cache,
+                                      request_ids: Sequence[str], positions: Sequence[int],
+                                      layer: int) -> torch.Tensor:
+    """The decode step's cache write and attention in one launch.
+
+    Same result, and the same pool bytes, as the reference's per-row
+    ``write_token(request_id, layer, position, key[b], value[b])`` loop
+    (pagedserve/attention/batched_paged_attention.py:115-124) followed by
+    ``triton_paged_decode_attention(query, cache, request_ids, positions,
+    layer)`` (:126-135): ``key``/``value`` are ``[B, Hkv, D]`` (or
+    ``[B, Hkv, 1, D]``) and row b lands at ``positions[b]``, the last position
+    the query attends to.  Runs as ``psb_paged_decode_append``.
+    """
+    if not query.is_cuda:
+        raise ValueError("B200 paged attention requires CUDA")
+    kv = cache.kv_cache
+    if key.ndim == 4:
+        key, value = key.squeeze(2), value.squeeze(2)
+    shape = (kv.num_kv_heads, kv.head_dim)
+    if tuple(key.shape[1:]) != shape or tuple(value.shape[1:]) != shape:
+        raise ValueError(f"Expected K/V shape {shape}; got key={tuple(key.shape)}, value={tuple(value.shape)}")
+    if key.dtype != kv.dtype or value.dtype != kv.dtype:
+        raise ValueError(f"K/V tensors must have dtype {kv.dtype}")
+    if key.shape[0] != query.shape[0] or value.shape[0] != query.shape[0]:
+        raise ValueError("Request IDs and positions must match batch size")
+    tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
     return ops.paged_decode(query, kv.k_cache, kv.v_cache, tables, lengths, layer,
-                            max_context=width * cache.block_size)
+                            max_context=width * cache.block_size, new_key=key, new_value=value)
 
 
 def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], layer: int, key: torch.Tensor,

@@ -54,6 +54,13 @@ struct DecodeParams {
   int32_t total_warps;  // warps of the fast-path decode grid
   int64_t max_units;
   int32_t* err;
+  // append (psb_paged_decode_append): row b's new K/V [Hkv, D] (element
+  // strides), stored at position ctx[b] - 1 before attending; null otherwise
+  const char* new_k;
+  const char* new_v;
+  int64_t nks, nkh, nvs, nvh;
+  char* k_pool_w;
+  char* v_pool_w;
 };
 
 // ---------------------------------------------------------------------------
@@ -501,6 +508,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   int32_t meta = 0;       // lane s: ring slot s flags (bit 0 data, then as in Chunk::meta)
   int32_t meta_seg = 0;   // lane s: sequence | head group << 20 of ring slot s
   int32_t meta_slot = 0;  // lane s: partial slot of ring slot s
+  int32_t meta_blk = 0;   // lane s: pool block of ring slot s
 
   // Copy one block (K and V of the HP packed heads, and the segment's q rows
   // with its first block) into the next ring slot as one cp.async group.
@@ -525,14 +533,32 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       const int64_t tile = zlayer + static_cast<int64_t>(blk) * p.hkv + shg * HP;
       const char* ksrc = reinterpret_cast<const char*>(kpool + tile * (16 * 64)) + lane * 16;
       const char* vsrc = reinterpret_cast<const char*>(vpool + tile * (16 * 64)) + lane * 16;
+      // Append: the sequence's new token is row valid - 1 of its last block.
+      // That row is copied straight from the caller's new K/V - the pool row
+      // is stale until the consume side stores it there from the ring - and
+      // only this warp reads this block in this launch.
+      const bool app = p.new_k != nullptr && ((mt >> 9) & 1);
+      const int r_new = valid - 1;
+      const char* nk = nullptr;
+      const char* nv = nullptr;
+      if (app) {
+        nk = p.new_k + (static_cast<int64_t>(sb) * p.nks + static_cast<int64_t>(shg * HP) * p.nkh) * sizeof(T);
+        nv = p.new_v + (static_cast<int64_t>(sb) * p.nvs + static_cast<int64_t>(shg * HP) * p.nvh) * sizeof(T);
+      }
       // a 16 x 64 tile is 2 KB = 128 chunks: 4 per lane, HP tiles per box;
-      // chunk lane + 32 i sits at row 4 i + lane / 8, so the swizzled column
-      // alternates between two per-lane values
+      // chunk lane + 32 i sits at row 4 (i % 4) + lane / 8 of tile i / 4, so
+      // the swizzled column alternates between two per-lane values
 #pragma unroll
       for (int i = 0; i < HP * 4; ++i) {
         const uint32_t d = sdst + i * 512 + ((i & 1) ? cp_dst_odd : cp_dst_even);
-        cp_async16_hint(d, ksrc + i * 512, stream_pol);
-        cp_async16_hint(d + Geo::kKV, vsrc + i * 512, stream_pol);
+        const char* ks = ksrc + i * 512;
+        const char* vs = vsrc + i * 512;
+        if (app && 4 * (i & 3) + (lane >> 3) == r_new) {
+          ks = nk + (i >> 2) * p.nkh * sizeof(T) + cp_col * 16;
+          vs = nv + (i >> 2) * p.nvh * sizeof(T) + cp_col * 16;
+        }
+        cp_async16_hint(d, ks, stream_pol);
+        cp_async16_hint(d + Geo::kKV, vs, stream_pol);
       }
     }
     if (first) {
@@ -554,6 +580,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       meta = (ok ? 1 : 0) | (mt & ~1);
       meta_seg = sg;
       meta_slot = sl;
+      meta_blk = blk;
     }
     ++issued;
     if (++ib == cur.n) {  // advance to the next chunk; build the one after it
@@ -598,6 +625,19 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     if (inflight >= 3) cp_async_wait<2>(); else if (inflight == 2) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncwarp();  // every lane's copies are visible to every lane
     const uint32_t sbase = smem_u32(ring + slot * Geo::kSlot);
+    if (p.new_k != nullptr && valid && ((mt >> 9) & 1)) {  // uniform over the warp
+      // append: store the new token's K/V rows, now in the ring (row r at
+      // r * 128, 16-byte column c at (c ^ r % 8) * 16 of its tile), into the
+      // pool; lane = (K | V) x head slot x column
+      const int32_t blk = __shfl_sync(0xffffffffu, meta_blk, slot);
+      const int kv = lane >> 4, hs = (lane >> 3) & 1, col = lane & 7, r_new = valid - 1;
+      if (hs < HP) {
+        const int64_t tile = zlayer + static_cast<int64_t>(blk) * p.hkv + ((cseg >> 20) & 0xff) * HP + hs;
+        const uint4 row = ld_shared_v4(sbase + kv * Geo::kKV + hs * kTileBytes + r_new * 128 +
+                                       ((col ^ (r_new & 7)) << 4));
+        *reinterpret_cast<uint4*>((kv ? p.v_pool_w : p.k_pool_w) + (tile * 16 + r_new) * 128 + col * 16) = row;
+      }
+    }
     if (first) {
       m_lo = m_hi = -INFINITY;
       l_lo = l_hi = 0.f;
@@ -990,6 +1030,34 @@ __global__ void __launch_bounds__(kThreads) decode_generic_kernel(const DecodePa
   }
 }
 
+// Append on the CUDA-core path: row b's new K/V at position ctx[b] - 1,
+// located through its block table as PagedKVCache.write_token does
+// (pagedserve/engine/paged_kv_cache.py:187-200), one element per thread;
+// launched before decode_generic_kernel on the same stream.
+template <typename T>
+__global__ void __launch_bounds__(256) append_rows_kernel(const DecodeParams p) {
+  const int D = p.head_dim, BS = p.block_size;
+  const int64_t per = static_cast<int64_t>(p.hkv) * D;
+  const int64_t total = per * p.batch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / per);
+    const int r = static_cast<int>(i - b * per);
+    const int h = r / D, d = r - h * D;
+    const int ctx = p.ctx[b];
+    if (ctx <= 0 || ctx > p.max_context) continue;  // no position to write (the decode flags bad lengths)
+    const int pos = ctx - 1;
+    const int blk = p.tables[static_cast<int64_t>(b) * p.table_stride + pos / BS];
+    if (blk < 0 || blk >= p.num_blocks) {
+      if (h == 0 && d == 0) flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
+      continue;
+    }
+    const int64_t off = (((static_cast<int64_t>(p.layer) * p.num_blocks + blk) * p.hkv + h) * BS + pos % BS) * D + d;
+    reinterpret_cast<T*>(p.k_pool_w)[off] = reinterpret_cast<const T*>(p.new_k)[b * p.nks + h * p.nkh + d];
+    reinterpret_cast<T*>(p.v_pool_w)[off] = reinterpret_cast<const T*>(p.new_v)[b * p.nvs + h * p.nvh + d];
+  }
+}
+
 size_t generic_smem_bytes(int group, int head_dim, int batch) {
   return sizeof(float) * static_cast<size_t>(GenericLayout(group, head_dim).ints) +
          sizeof(int32_t) * (2 * static_cast<size_t>(batch) + 1);
@@ -1091,6 +1159,11 @@ int launch_generic(const DecodeParams& prm, cudaStream_t stream, int sms) {
   if (!kernel_occupancy(kern, kThreads, smem, &occ)) return PSB_ERR_CUDA;
   const int64_t grid = std::min<int64_t>(prm.max_units, static_cast<int64_t>(sms) * std::max(occ, 1));
   discard_stale_error();
+  if (prm.new_k != nullptr) {
+    const int64_t elems = static_cast<int64_t>(prm.batch) * prm.hkv * prm.head_dim;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((elems + 255) / 256, static_cast<int64_t>(sms) * 8));
+    append_rows_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(prm);
+  }
   decode_generic_kernel<T><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(prm);
   return check_launch();
 }
@@ -1147,13 +1220,18 @@ extern "C" int psb_paged_decode_workspace_init(void* workspace, size_t workspace
   return PSB_OK;
 }
 
-extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
-                                int64_t o_stride_b, int64_t o_stride_h, const void* k_cache, const void* v_cache,
-                                const int32_t* block_tables, int64_t table_stride, const int32_t* context_lens,
-                                int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers,
-                                int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
-                                int32_t dtype, int32_t max_context, float scale, void* workspace,
-                                size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream) {
+namespace psb {
+namespace {
+
+// psb_paged_decode, and with new_key != nullptr psb_paged_decode_append.
+int paged_decode_impl(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out, int64_t o_stride_b,
+                      int64_t o_stride_h, const void* k_cache, const void* v_cache, const void* new_key,
+                      int64_t key_stride_b, int64_t key_stride_h, const void* new_value, int64_t value_stride_b,
+                      int64_t value_stride_h, const int32_t* block_tables, int64_t table_stride,
+                      const int32_t* context_lens, int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers,
+                      int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype,
+                      int32_t max_context, float scale, void* workspace, size_t workspace_bytes, int32_t* error_flag,
+                      psb_stream_t stream) {
   if (!query || !out || !k_cache || !v_cache || !block_tables || !context_lens) return PSB_ERR_INVALID;
   if (batch <= 0 || q_heads <= 0 || num_kv_heads <= 0 || q_heads % num_kv_heads || head_dim <= 0 ||
       block_size <= 0 || num_blocks <= 0 || num_layers <= 0 || layer < 0 || layer >= num_layers ||
@@ -1162,13 +1240,20 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   if (dtype != PSB_F32 && dtype != PSB_F16 && dtype != PSB_BF16) return PSB_ERR_INVALID;
   if (static_cast<int64_t>(num_layers) * num_blocks * num_kv_heads >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
   const int group = q_heads / num_kv_heads;
-  const int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, max_context, query, q_stride_b,
-                             q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache);
+  int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, max_context, query, q_stride_b,
+                       q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache);
+  if (new_key != nullptr) {
+    // the fast path copies new rows in 16-byte pieces
+    const bool rows16 = key_stride_b % 8 == 0 && key_stride_h % 8 == 0 && value_stride_b % 8 == 0 &&
+                        value_stride_h % 8 == 0 && reinterpret_cast<uintptr_t>(new_key) % 16 == 0 &&
+                        reinterpret_cast<uintptr_t>(new_value) % 16 == 0;
+    if (!rows16) hp = 0;
+  }
   const int sms = device_sm_count();
   if (sms <= 0) return PSB_ERR_CUDA;
   if (workspace == nullptr) return PSB_ERR_WORKSPACE;
 
-  DecodeParams p;
+DecodeParams p;
   p.q = static_cast<const char*>(query);
   p.qsb = q_stride_b;
   p.qsh = q_stride_h;
@@ -1193,6 +1278,14 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = error_flag;
   p.total_warps = 0;
+  p.new_k = static_cast<const char*>(new_key);
+  p.new_v = static_cast<const char*>(new_value);
+  p.nks = key_stride_b;
+  p.nkh = key_stride_h;
+  p.nvs = value_stride_b;
+  p.nvh = value_stride_h;
+  p.k_pool_w = const_cast<char*>(static_cast<const char*>(k_cache));
+  p.v_pool_w = const_cast<char*>(static_cast<const char*>(v_cache));
   char* ws = static_cast<char*>(workspace);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (hp) {
@@ -1223,4 +1316,37 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
     case PSB_F16: return launch_generic<__half>(p, s, sms);
     default: return launch_generic<float>(p, s, sms);
   }
+}
+
+}  // namespace
+}  // namespace psb
+
+extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
+                                int64_t o_stride_b, int64_t o_stride_h, const void* k_cache, const void* v_cache,
+                                const int32_t* block_tables, int64_t table_stride, const int32_t* context_lens,
+                                int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers,
+                                int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                                int32_t dtype, int32_t max_context, float scale, void* workspace,
+                                size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream) {
+  return paged_decode_impl(query, q_stride_b, q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache, nullptr, 0, 0,
+                           nullptr, 0, 0, block_tables, table_stride, context_lens, batch, q_heads, layer, num_layers,
+                           num_blocks, num_kv_heads, block_size, head_dim, dtype, max_context, scale, workspace,
+                           workspace_bytes, error_flag, stream);
+}
+
+extern "C" int psb_paged_decode_append(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
+                                       int64_t o_stride_b, int64_t o_stride_h, void* k_cache, void* v_cache,
+                                       const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
+                                       const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
+                                       const int32_t* block_tables, int64_t table_stride, const int32_t* context_lens,
+                                       int32_t batch, int32_t q_heads, int32_t layer, int32_t num_layers,
+                                       int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                                       int32_t dtype, int32_t max_context, float scale, void* workspace,
+                                       size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream) {
+  if (!new_key || !new_value) return PSB_ERR_INVALID;
+  return paged_decode_impl(query, q_stride_b, q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache, new_key,
+                           key_stride_b, key_stride_h, new_value, value_stride_b, value_stride_h, block_tables,
+                           table_stride, context_lens, batch, q_heads, layer, num_layers, num_blocks, num_kv_heads,
+                           block_size, head_dim, dtype, max_context, scale, workspace, workspace_bytes, error_flag,
+                           stream);
 }

@@ -129,11 +129,15 @@ def decode_workspace_bytes(batch: int, q_heads: int, hkv: int, head_dim: int, bl
 def paged_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                  context_lens: torch.Tensor, layer: int, scale: float | None = None, out: torch.Tensor | None = None,
                  max_context: int | None = None, workspace: torch.Tensor | None = None,
-                 error_flag: torch.Tensor | None = None) -> torch.Tensor:
+                 error_flag: torch.Tensor | None = None, new_key: torch.Tensor | None = None,
+                 new_value: torch.Tensor | None = None) -> torch.Tensor:
     """Decode attention for ``query [B, Hq, D]`` (or ``[B, Hq, 1, D]``) over the paged pool.
 
     ``block_tables [B, M]`` int32 and ``context_lens [B]`` int32 live on the
     device; ``max_context`` (default ``M * block_size``) bounds every length.
+    With ``new_key`` / ``new_value`` (``[B, Hkv, D]`` or ``[B, Hkv, 1, D]``)
+    the same launch first stores row b's new token at position
+    ``context_lens[b] - 1`` through its block table (psb_paged_decode_append).
     Returns ``out`` with ``query``'s shape and dtype.
     """
     _require_cuda(query, k_cache, v_cache, block_tables, context_lens)
@@ -171,6 +175,23 @@ def paged_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if workspace is None:
         workspace = DecodeWorkspace.for_device(query.device).get(need, bsz, hkv)
     lib = _native.load()
+    if (new_key is None) != (new_value is None):
+        raise ValueError("new_key and new_value go together")
+    if new_key is not None:
+        _require_cuda(new_key, new_value)
+        nk = new_key.squeeze(2) if new_key.ndim == 4 else new_key
+        nv = new_value.squeeze(2) if new_value.ndim == 4 else new_value
+        for t in (nk, nv):
+            if t.shape != (bsz, hkv, d) or t.dtype != q3.dtype or t.stride(2) != 1:
+                raise ValueError(f"new K/V must be [{bsz}, {hkv}, {d}] {q3.dtype} with unit stride along head_dim")
+        _native.check(lib.psb_paged_decode_append(
+            q3.data_ptr(), q3.stride(0), q3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1), k_cache.data_ptr(),
+            v_cache.data_ptr(), nk.data_ptr(), nk.stride(0), nk.stride(1), nv.data_ptr(), nv.stride(0), nv.stride(1),
+            block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), bsz, hq, layer, nl, nb, hkv, bs,
+            d, dtype_code(q3.dtype), int(max_context), scale, workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), _ptr(error_flag), _stream(query.device)),
+            "paged_decode_append")
+        return out
     _native.check(lib.psb_paged_decode(
         q3.data_ptr(), q3.stride(0), q3.stride(1), o3.data_ptr(), o3.stride(0), o3.stride(1), k_cache.data_ptr(),
         v_cache.data_ptr(), block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), bsz, hq, layer,
