@@ -422,7 +422,9 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <typename T, int HP>
+// APPEND: psb_paged_decode_append (the new-token store below); a separate
+// instantiation so plain decode carries none of it.
+template <typename T, int HP, bool APPEND>
 __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const DecodeParams p) {
   using Geo = FastGeom<HP>;
   extern __shared__ uint8_t smem_raw[];
@@ -537,7 +539,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       // That row is copied straight from the caller's new K/V - the pool row
       // is stale until the consume side stores it there from the ring - and
       // only this warp reads this block in this launch.
-      const bool app = p.new_k != nullptr && ((mt >> 9) & 1);
+      const bool app = APPEND && ((mt >> 9) & 1);
       const int r_new = valid - 1;
       const char* nk = nullptr;
       const char* nv = nullptr;
@@ -548,17 +550,26 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
       // a 16 x 64 tile is 2 KB = 128 chunks: 4 per lane, HP tiles per box;
       // chunk lane + 32 i sits at row 4 (i % 4) + lane / 8 of tile i / 4, so
       // the swizzled column alternates between two per-lane values
+      if (!app) {  // warp-uniform: only a sequence's last block takes the other loop
 #pragma unroll
-      for (int i = 0; i < HP * 4; ++i) {
-        const uint32_t d = sdst + i * 512 + ((i & 1) ? cp_dst_odd : cp_dst_even);
-        const char* ks = ksrc + i * 512;
-        const char* vs = vsrc + i * 512;
-        if (app && 4 * (i & 3) + (lane >> 3) == r_new) {
-          ks = nk + (i >> 2) * p.nkh * sizeof(T) + cp_col * 16;
-          vs = nv + (i >> 2) * p.nvh * sizeof(T) + cp_col * 16;
+        for (int i = 0; i < HP * 4; ++i) {
+          const uint32_t d = sdst + i * 512 + ((i & 1) ? cp_dst_odd : cp_dst_even);
+          cp_async16_hint(d, ksrc + i * 512, stream_pol);
+          cp_async16_hint(d + Geo::kKV, vsrc + i * 512, stream_pol);
         }
-        cp_async16_hint(d, ks, stream_pol);
-        cp_async16_hint(d + Geo::kKV, vs, stream_pol);
+      } else {
+#pragma unroll
+        for (int i = 0; i < HP * 4; ++i) {
+          const uint32_t d = sdst + i * 512 + ((i & 1) ? cp_dst_odd : cp_dst_even);
+          const char* ks = ksrc + i * 512;
+          const char* vs = vsrc + i * 512;
+          if (4 * (i & 3) + (lane >> 3) == r_new) {
+            ks = nk + (i >> 2) * p.nkh * sizeof(T) + cp_col * 16;
+            vs = nv + (i >> 2) * p.nvh * sizeof(T) + cp_col * 16;
+          }
+          cp_async16_hint(d, ks, stream_pol);
+          cp_async16_hint(d + Geo::kKV, vs, stream_pol);
+        }
       }
     }
     if (first) {
@@ -625,7 +636,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     if (inflight >= 3) cp_async_wait<2>(); else if (inflight == 2) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncwarp();  // every lane's copies are visible to every lane
     const uint32_t sbase = smem_u32(ring + slot * Geo::kSlot);
-    if (p.new_k != nullptr && valid && ((mt >> 9) & 1)) {  // uniform over the warp
+    if (APPEND && valid && ((mt >> 9) & 1)) {  // uniform over the warp
       // append: store the new token's K/V rows, now in the ring (row r at
       // r * 128, 16-byte column c at (c ^ r % 8) * 16 of its tile), into the
       // pool; lane = (K | V) x head slot x column
@@ -1128,9 +1139,11 @@ template <typename T, int HP>
 int launch_fast(DecodeParams prm, cudaStream_t stream, int max_ctas) {
   const size_t smem = FastGeom<HP>::bytes(prm.batch);
   if (smem > 227 * 1024) return PSB_ERR_UNSUPPORTED;
-  const void* kern = reinterpret_cast<const void*>(decode_fast_kernel<T, HP>);
+  const bool append = prm.new_k != nullptr;
+  const auto kernel = append ? decode_fast_kernel<T, HP, true> : decode_fast_kernel<T, HP, false>;
   int occ = 0;
-  if (!kernel_occupancy(kern, kFastThreads, smem, &occ) || occ < 1) return PSB_ERR_CUDA;
+  if (!kernel_occupancy(reinterpret_cast<const void*>(kernel), kFastThreads, smem, &occ) || occ < 1)
+    return PSB_ERR_CUDA;
   // an upper bound of the items from the host-known maximum context; small
   // batches get fewer CTAs so each warp streams at least kFastMinBlocks blocks
   const int64_t max_items = static_cast<int64_t>(prm.batch) * (prm.hkv / HP) *
@@ -1139,8 +1152,7 @@ int launch_fast(DecodeParams prm, cudaStream_t stream, int max_ctas) {
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_ctas)));
   prm.total_warps = grid * kFastWarps;
   discard_stale_error();
-  cudaError_t e = launch_pdl(decode_fast_kernel<T, HP>, dim3(static_cast<unsigned>(grid)), dim3(kFastThreads), smem,
-                             stream, prm);
+  cudaError_t e = launch_pdl(kernel, dim3(static_cast<unsigned>(grid)), dim3(kFastThreads), smem, stream, prm);
   if (e != cudaSuccess) return record_cuda_error(e);
   const int64_t merges = static_cast<int64_t>(prm.batch) * (prm.hkv / HP);
   if (!prefer_max_shared(reinterpret_cast<const void*>(decode_combine_kernel<T, HP>))) return PSB_ERR_CUDA;
