@@ -50,8 +50,9 @@ METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s); decode tok/s at 1/2/4/8 B20
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# DRAM bytes of one decode + combine launch on the rank-0 workload, measured with ncu
-DECODE_TRAFFIC_BYTES = 198_700_000
+# DRAM bytes of one fused decode step (decode with the new-token store + combine)
+# on the rank-0 workload, measured with ncu
+STEP_TRAFFIC_BYTES = 196_300_000
 
 
 def context_lengths(seed: int, n: int = BATCH) -> np.ndarray:
@@ -345,14 +346,14 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | None = None):
+def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | None = None, layers: int = LAYERS):
     from pagedserve_b200 import PagedKVCache
     rng = np.random.default_rng(seed + 7)
     lens = context_lengths(seed) if lens is None else lens
     batch = len(lens)
     need = int(np.sum(-(-lens // BS)))
     nb = int(math.ceil(SLACK * need))
-    cache = PagedKVCache(num_blocks=nb, num_layers=LAYERS, num_kv_heads=HKV, head_dim=D, block_size=BS,
+    cache = PagedKVCache(num_blocks=nb, num_layers=layers, num_kv_heads=HKV, head_dim=D, block_size=BS,
                          dtype=torch.bfloat16, device=device, free_order=rng.permutation(nb))
     ids = [f"seq-{i}" for i in range(batch)]
     for rid, n in zip(ids, lens):
@@ -383,7 +384,8 @@ def run_b200(args, world, rank, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
         pg = dist
 
-    w = build_device_workload(1000 + rank, device, rank_lengths(world, rank))
+    LAYERS = args.layers
+    w = build_device_workload(1000 + rank, device, rank_lengths(world, rank), LAYERS)
     batch = len(w["lens"])
     k, v = w["cache"].kv_cache.k_cache, w["cache"].kv_cache.v_cache
     out = torch.empty_like(w["q"])
@@ -519,7 +521,7 @@ def run_b200(args, world, rank, local):
     from pagedserve_b200.sharding import aggregate_counters
     lens = w["lens"]
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
-    rank_dec_ms = dec_ms
+    rank_step_ms = step_ms
     times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
                                 "two_ms": two_ms}, device, op="max")
     work = aggregate_counters({"bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())}, device, op="sum")
@@ -529,7 +531,7 @@ def run_b200(args, world, rank, local):
     value = total_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
-    achieved = decode_bytes(lens) / (rank_dec_ms * 1e-3) / 1e9
+    achieved = step_bytes / (rank_step_ms * 1e-3) / 1e9
 
     if rank == 0:
         cpu = cpu_baseline(0) if world == 1 else None
@@ -537,15 +539,16 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) KV/Q, lognormal contexts)",
-            "config": {"workload": "serving-scale paged decode + reshape_and_cache: 256 x N_gpus requests, ctx "
+            "config": {"layers": LAYERS,
+                       "workload": "serving-scale paged decode + reshape_and_cache: 256 x N_gpus requests, ctx "
                                    "lognormal(median 1024, sigma 0.8) clipped [16, 8192], placed on the GPUs in "
                                    "arrival order by most free KV blocks; 14q/2kv heads, d64, block 16, pool 1.25x "
                                    "need per GPU, shuffled blocks",
                        "sequences": total_seqs, "sum_ctx": int(work["ctx"]), "bytes_per_step": int(total_bytes),
                        "rank0_sequences": batch, "rank0_sum_ctx": int(lens.sum()),
-                       "l2": "inputs larger than L2: a 24-layer pool, consecutive steps are consecutive "
+                       "l2": f"inputs larger than L2: a {LAYERS}-layer pool, consecutive steps are consecutive "
                              "layers (~180 MB of KV each, read with an evict-first L2 policy)",
-                       "launch": "one CUDA graph per decode iteration: 24 layer calls, each the fused decode "
+                       "launch": f"one CUDA graph per decode iteration: {LAYERS} layer calls, each the fused decode "
                                  "step (new token stored through the block table + split-K attention, then the "
                                  "combine), chained by programmatic dependent launch; a step is one layer call",
                        "per_layer_graph_ms": round(single_ms, 5),
@@ -558,19 +561,21 @@ def run_b200(args, world, rank, local):
             "attn_layer_tok_per_s": round(total_seqs / (step_ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "decode_fast_kernel<bf16, 2> + decode_combine_kernel",
-                         "timing": "CUDA events around K decode+combine layer calls in decode-only iteration "
-                                   "graphs; average per layer call",
-                         "bytes_per_launch": decode_bytes(lens),
-                         "avg_launch_ms": round(dec_ms, 5), "traffic": DECODE_TRAFFIC_BYTES,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode "
-                                           "(193.9 MB) and one combine (4.8 MB) launch on this seeded workload "
-                                           "(decode ncu summary under profiles/)"},
+                         "kernel": "decode_fast_kernel<bf16, 2, append> + decode_combine_kernel (the fused step)",
+                         "timing": "CUDA events around the K layer calls (iteration graphs) on this rank; average "
+                                   "per layer call",
+                         "bytes_per_launch": step_bytes,
+                         "avg_launch_ms": round(rank_step_ms, 5), "traffic": STEP_TRAFFIC_BYTES,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused decode "
+                                           "(187.5 + 4.0 MB) and one combine (4.8 MB) launch on this seeded "
+                                           "workload (decode ncu summary under profiles/)",
+                         "decode_only_ms": round(dec_ms, 5),
+                         "decode_only_note": "decode + combine without the new-token store, same graphs"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
                     "path": "per layer call: q, new k, new v copied from pinned host buffers, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
-                            "one launch), output copied back; block tables built and copied once per 24-layer "
+                            f"one launch), output copied back; block tables built and copied once per {LAYERS}-layer "
                             "iteration"},
             "gpu_launches": 2 * args.steps,
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
@@ -593,8 +598,14 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers in the pool and the iteration graph (default: the model's 24); every step is "
+                         "still one full layer call, so fewer only shrink the device memory a profiler must "
+                         "save and restore")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.layers < 2:
+        ap.error("--layers must be at least 2 (consecutive steps must not reuse one layer's KV from L2)")
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
