@@ -132,6 +132,36 @@ int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q_stride_h, 
                      void* workspace, size_t workspace_bytes, int32_t* error_flag, psb_stream_t stream);
 
 /*
+ * rope_reshape_and_cache: rotary position embedding of q and k fused with the
+ * slot-mapped K/V write.
+ *
+ * Replaces the transformers Qwen2 apply_rotary_pos_emb the reference applies
+ * in its decode glue (pagedserve/attention/batched_paged_attention.py:105-112,
+ * imported at :8) followed by the per-row write_token loop (:115-124):
+ *     q'[t, h] = q[t, h] * cos[t] + rotate_half(q[t, h]) * sin[t]   (k' likewise),
+ *     rotate_half(x) = cat(-x[D/2:], x[:D/2]),
+ * then, for slot s = slot_mapping[t] >= 0, k'[t] and value[t] stored as
+ * psb_reshape_and_cache stores them.  cos/sin are per-token rows
+ * [num_tokens, head_dim] (row stride ``cs_stride_t`` elements; the engine's
+ * position embeddings, pagedserve/model/engine.py:572-575).  Products and sums
+ * are evaluated in fp32 and rounded to ``dtype`` as PyTorch evaluates that
+ * expression, so query_out, key_out and the pool bytes are bit-identical to
+ * the reference's.  query [num_tokens, num_q_heads, head_dim] -> query_out
+ * (either query itself, for in place, or not overlapping it); key_out may be
+ * null (the rotated keys then go only to the pool).  head_dim must be even.
+ * A slot past the pool is skipped and flagged (PSB_DEVERR_SLOT_RANGE).  A
+ * programmatic dependent launch, like psb_reshape_and_cache.
+ */
+int psb_rope_reshape_and_cache(const void* query, int64_t q_stride_t, int64_t q_stride_h, void* query_out,
+                               int64_t qo_stride_t, int64_t qo_stride_h, const void* key, int64_t k_stride_t,
+                               int64_t k_stride_h, void* key_out, int64_t ko_stride_t, int64_t ko_stride_h,
+                               const void* value, int64_t v_stride_t, int64_t v_stride_h, const void* cos,
+                               const void* sin, int64_t cs_stride_t, void* k_cache, void* v_cache,
+                               const int64_t* slot_mapping, int32_t num_tokens, int32_t num_q_heads, int32_t layer,
+                               int32_t num_layers, int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                               int32_t head_dim, int32_t dtype, int32_t* error_flag, psb_stream_t stream);
+
+/*
  * paged_decode_append: the decode step's cache write and attention in one
  * launch.  Equivalent to writing row b's new key/value
  * ([batch, num_kv_heads, head_dim], element strides (stride_b, stride_h),

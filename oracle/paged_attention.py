@@ -22,6 +22,8 @@ Reference functions restated (paths inside the PagedServe project):
 * ``write_tokens``       <- pagedserve/engine/paged_kv_cache.py:187-200
 * ``slot_for``           <- pagedserve/engine/paged_kv_cache.py:187-192
 * ``padded_block_table`` <- pagedserve/attention/triton_paged_decode.py:134-154
+* ``apply_rope``         <- pagedserve/attention/batched_paged_attention.py:105-112
+                            (transformers Qwen2 ``apply_rotary_pos_emb``, imported at :8)
 
 Two numeric modes are offered.  ``mode="exact"`` computes in float64 from the
 stored values: this is the "fp32 reference" the bf16 kernels are held to
@@ -298,6 +300,38 @@ def reshape_and_cache(key: np.ndarray, value: np.ndarray, k_cache: np.ndarray, v
             continue
         k_cache[layer, s // bs, :, s % bs, :] = key[t]
         v_cache[layer, s // bs, :, s % bs, :] = value[t]
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, dtype: str) -> np.ndarray:
+    """Rotary position embedding of ``x [T, H, D]`` with per-token ``cos, sin
+    [T, D]``, as the reference's decode glue applies it
+    (pagedserve/attention/batched_paged_attention.py:105-112, the transformers
+    Qwen2 ``apply_rotary_pos_emb``: ``x * cos + rotate_half(x) * sin`` with
+    ``rotate_half(x) = cat(-x2, x1)``), rounded as PyTorch does for ``dtype``
+    tensors: each product and the sum are computed in fp32 and rounded to
+    ``dtype``.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    c = np.asarray(cos, dtype=np.float32)[:, None, :]
+    s = np.asarray(sin, dtype=np.float32)[:, None, :]
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    a = round_to(x * c, dtype)
+    b = round_to(rot * s, dtype)
+    return round_to(a + b, dtype)
+
+
+def rope_reshape_and_cache(query: np.ndarray, key: np.ndarray, value: np.ndarray, cos: np.ndarray, sin: np.ndarray,
+                           k_cache: np.ndarray, v_cache: np.ndarray, slots: np.ndarray, layer: int,
+                           dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """The decode glue's RoPE followed by its per-row ``write_token`` loop
+    (batched_paged_attention.py:105-124), over a slot mapping: returns the
+    rotated ``(query, key)`` and writes the rotated key and the value into the
+    pools in place (negative slot = no write)."""
+    q_rot = apply_rope(query, cos, sin, dtype)
+    k_rot = apply_rope(key, cos, sin, dtype)
+    reshape_and_cache(k_rot, np.asarray(value, dtype=np.float32), k_cache, v_cache, slots, layer)
+    return q_rot, k_rot
 
 
 # --------------------------------------------------------------------------

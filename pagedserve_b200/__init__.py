@@ -6,6 +6,7 @@ Public surface:
   (pagedserve/attention/triton_paged_decode.py:98)
 * ``write_tokens`` - batched replacement of the per-row ``write_token`` loop
 * ``paged_decode_attention_with_write`` - both in one launch
+* ``rope_and_write_tokens`` - the glue's rotary embedding fused with the write
 * ``ops.reshape_and_cache / paged_decode / varlen_prefill / pack_step`` -
   tensor-level API over the C ABI (include/pagedserve_b200.h)
 * ``PagedKVCache`` and friends - host-side block bookkeeping with the
@@ -15,10 +16,11 @@ Public surface:
 """
 
 from . import ops
-from .attention import paged_decode_attention, paged_decode_attention_with_write, write_tokens
+from .attention import (paged_decode_attention, paged_decode_attention_with_write, rope_and_write_tokens,
+                        write_tokens)
 from .paged_kv import BlockManager, BlockTable, KVCache, PagedKVCache
 from .sharding import SequenceDispatcher
 
-__all__ = ["ops", "paged_decode_attention", "paged_decode_attention_with_write", "write_tokens", "BlockManager",
-           "BlockTable", "KVCache", "PagedKVCache", "SequenceDispatcher"]
+__all__ = ["ops", "paged_decode_attention", "paged_decode_attention_with_write", "rope_and_write_tokens",
+           "write_tokens", "BlockManager", "BlockTable", "KVCache", "PagedKVCache", "SequenceDispatcher"]
 __version__ = "0.1.0"

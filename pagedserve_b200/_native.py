@@ -42,6 +42,10 @@ SIGNATURES = {
     "psb_paged_decode": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32,
         _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p, _sz, _c_void_p, _c_void_p]),
+    "psb_rope_reshape_and_cache": (ctypes.c_int, [
+        _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64,
+        _i64, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i64, _i32, _i32,
+        _i32, _i32, _c_void_p, _c_void_p]),
     "psb_paged_decode_append": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64,
         _i64, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32,

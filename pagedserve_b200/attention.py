@@ -186,16 +186,52 @@ def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], la
     if key.dtype != kv.dtype or value.dtype != kv.dtype:
         raise ValueError(f"K/V tensors must have dtype {kv.dtype}")
 
+    slot_t = _slots(cache, request_ids, positions, key.device)
+    ops.reshape_and_cache(key, value, kv.k_cache, kv.v_cache, slot_t, layer)
+
+
+def rope_and_write_tokens(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, cos: torch.Tensor,
+                          sin: torch.Tensor, cache, request_ids: Sequence[str], positions: Sequence[int],
+                          layer: int) -> torch.Tensor:
+    """The decode glue's rotary embedding and KV write in one launch.
+
+    Replaces ``apply_rotary_pos_emb(query, key, cos, sin)`` followed by the
+    per-row ``write_token`` loop (pagedserve/attention/batched_paged_attention.py:105-124):
+    ``query [B, Hq, 1, D]``, ``key``/``value [B, Hkv, 1, D]`` as the glue
+    holds them, ``cos``/``sin`` the engine's position embeddings (one
+    ``[D]`` row per batch row).  Writes the rotated key and the value of row b
+    at ``positions[b]`` and returns the rotated query, bit-identical to the
+    reference's (psb_rope_reshape_and_cache).
+    """
+    kv = cache.kv_cache
+    if query.ndim != 4 or query.shape[2] != 1:
+        raise ValueError("query must have shape [B, Hq, 1, D]")
+    batch = query.shape[0]
+    if key.ndim == 4:
+        key, value = key.squeeze(2), value.squeeze(2)
+    shape = (kv.num_kv_heads, kv.head_dim)
+    if tuple(key.shape[1:]) != shape or tuple(value.shape[1:]) != shape or key.shape[0] != batch:
+        raise ValueError(f"Expected K/V shape {shape}; got key={tuple(key.shape)}, value={tuple(value.shape)}")
+    if len(request_ids) != batch or len(positions) != batch:
+        raise ValueError("Request IDs and positions must match batch size")
+    slot_t = _slots(cache, request_ids, positions, key.device)
+    q_rot, _ = ops.rope_reshape_and_cache(query.squeeze(2), key, value, cos.reshape(batch, -1),
+                                          sin.reshape(batch, -1), kv.k_cache, kv.v_cache, slot_t, layer,
+                                          key_out=False)
+    return q_rot.unsqueeze(2)
+
+
+def _slots(cache, request_ids, positions, device):
+    """Device int64 slots of (request, position) pairs, reused within an epoch."""
     def build():
         slots = np.fromiter((cache.slot_of(r, p) if hasattr(cache, "slot_of") else _slot(cache, r, p)
                              for r, p in zip(request_ids, positions)), dtype=np.int64, count=len(request_ids))
         host = torch.from_numpy(slots)
-        if key.device.type == "cuda":
+        if device.type == "cuda":
             host = host.pin_memory()
-        return host.to(key.device, non_blocking=True)
+        return host.to(device, non_blocking=True)
 
-    slot_t = _memo(cache, "slots", request_ids, positions, key.device, build)
-    ops.reshape_and_cache(key, value, kv.k_cache, kv.v_cache, slot_t, layer)
+    return _memo(cache, "slots", request_ids, positions, device, build)
 
 
 def _slot(cache, request_id: str, position: int) -> int:

@@ -1,0 +1,241 @@
+// rope_reshape_and_cache: the rotary position embedding of q and k fused with
+// the slot-mapped K/V write, one launch per layer.
+//
+// Replaces, in the reference's decode glue, the transformers Qwen2
+// ``apply_rotary_pos_emb`` (imported at
+// pagedserve/attention/batched_paged_attention.py:8, applied at :105-112)
+// followed by the per-row ``write_token`` loop (:115-124):
+//     q' = q * cos + rotate_half(q) * sin,  k' likewise,
+//     rotate_half(x) = cat(-x[D/2:], x[:D/2]),
+//     cache[layer, slot / BS, h, slot % BS, :] = k'[t, h, :]  (and v[t, h, :]).
+// cos/sin are the caller's per-token rows (the engine's position embeddings,
+// pagedserve/model/engine.py:572-575), so the angles are the reference's own.
+// Every product and the sum are evaluated in fp32 and rounded to the storage
+// type, as PyTorch evaluates that expression on bf16/f16 tensors, so q', k'
+// and the pool bytes are bit-identical to the reference's.  A thread rotates
+// one VEC-element piece of each half of one head (the two halves meet in the
+// rotation), 16-byte accesses when rows allow.
+#include <algorithm>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace psb {
+namespace {
+
+struct RopeParams {
+  const char* q;
+  int64_t qst, qsh;  // bytes
+  char* qo;
+  int64_t qost, qosh;
+  const char* k;
+  int64_t kst, ksh;
+  char* ko;  // may be null
+  int64_t kost, kosh;
+  const char* v;
+  int64_t vst, vsh;
+  const char* cos;
+  const char* sin;
+  int64_t cst;
+  char* kc;
+  char* vc;
+  const int64_t* slots;
+  int32_t tokens, hq, hkv, block_size, head_dim;
+  int64_t layer_base_tiles, pool_slots;
+  int32_t* err;
+};
+
+// VEC consecutive elements, moved as one 16-byte access when VEC * sizeof(T) == 16
+template <typename T, int VEC>
+struct Piece {
+  alignas(VEC * sizeof(T) == 16 ? 16 : alignof(T)) T e[VEC];
+  __device__ __forceinline__ void load(const char* src) {
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(e) = __ldg(reinterpret_cast<const uint4*>(src));
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) e[i] = reinterpret_cast<const T*>(src)[i];
+    }
+  }
+  __device__ __forceinline__ void store(char* dst) const {
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(e);
+    } else {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) reinterpret_cast<T*>(dst)[i] = e[i];
+    }
+  }
+};
+
+// x rounded to T and back (the identity for fp32)
+template <typename T>
+__device__ __forceinline__ float rnd(float x) {
+  return Elem<T>::to_float(Elem<T>::from_float(x));
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) rope_cache_kernel(const RopeParams p) {
+  // a programmatic dependent, like reshape_and_cache: the next kernel may
+  // launch now; this one waits for its predecessor before touching memory
+  pdl_launch_dependents();
+  pdl_wait();
+  const int half = p.head_dim / 2;
+  const int pieces = half / VEC;
+  const int heads = p.hq + 2 * p.hkv;
+  const int64_t per_tok = static_cast<int64_t>(heads) * pieces;
+  const int64_t total = per_tok * p.tokens;
+  const int64_t hb = static_cast<int64_t>(half) * sizeof(T);  // byte offset of the second half
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / per_tok;
+    const int r = static_cast<int>(i - t * per_tok);
+    const int hs = r / pieces;
+    const int64_t e0 = static_cast<int64_t>(r - hs * pieces) * VEC * sizeof(T);  // byte offset in the first half
+    const bool is_q = hs < p.hq, is_k = !is_q && hs < p.hq + p.hkv;
+    // the pool slot (keys and values only)
+    int64_t dst = -1;
+    if (!is_q) {
+      const int h = is_k ? hs - p.hq : hs - p.hq - p.hkv;
+      const int64_t s = __ldg(p.slots + t);
+      if (s >= p.pool_slots) {
+        if (h == 0 && e0 == 0 && is_k) flag_error(p.err, PSB_DEVERR_SLOT_RANGE);
+      } else if (s >= 0) {
+        const int64_t blk = s / p.block_size, off = s - blk * p.block_size;
+        dst = (((p.layer_base_tiles + blk * p.hkv + h) * p.block_size + off) * p.head_dim) * sizeof(T) + e0;
+      }
+    }
+    if (!is_q && !is_k) {  // value: copied unchanged
+      const int h = hs - p.hq - p.hkv;
+      if (dst < 0) continue;
+      const char* src = p.v + t * p.vst + h * p.vsh + e0;
+      Piece<T, VEC> a, b;
+      a.load(src);
+      b.load(src + hb);
+      a.store(p.vc + dst);
+      b.store(p.vc + dst + hb);
+      continue;
+    }
+    const int h = is_q ? hs : hs - p.hq;
+    const char* src = is_q ? p.q + t * p.qst + h * p.qsh + e0 : p.k + t * p.kst + h * p.ksh + e0;
+    const char* cs = p.cos + t * p.cst + e0;
+    const char* sn = p.sin + t * p.cst + e0;
+    Piece<T, VEC> x1, x2, c1, c2, s1, s2;
+    x1.load(src);
+    x2.load(src + hb);
+    c1.load(cs);
+    c2.load(cs + hb);
+    s1.load(sn);
+    s2.load(sn + hb);
+    Piece<T, VEC> o1, o2;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float a = Elem<T>::to_float(x1.e[j]), b = Elem<T>::to_float(x2.e[j]);
+      // first half: x1 cos - x2 sin; second half: x2 cos + x1 sin
+      o1.e[j] = Elem<T>::from_float(__fadd_rn(rnd<T>(__fmul_rn(a, Elem<T>::to_float(c1.e[j]))),
+                                              rnd<T>(__fmul_rn(-b, Elem<T>::to_float(s1.e[j])))));
+      o2.e[j] = Elem<T>::from_float(__fadd_rn(rnd<T>(__fmul_rn(b, Elem<T>::to_float(c2.e[j]))),
+                                              rnd<T>(__fmul_rn(a, Elem<T>::to_float(s2.e[j])))));
+    }
+    if (is_q) {
+      char* out = p.qo + t * p.qost + h * p.qosh + e0;
+      o1.store(out);
+      o2.store(out + hb);
+      continue;
+    }
+    if (p.ko != nullptr) {
+      char* out = p.ko + t * p.kost + h * p.kosh + e0;
+      o1.store(out);
+      o2.store(out + hb);
+    }
+    if (dst >= 0) {
+      o1.store(p.kc + dst);
+      o2.store(p.kc + dst + hb);
+    }
+  }
+}
+
+template <typename T, int VEC>
+int launch_rope(const RopeParams& p, cudaStream_t s, int sms) {
+  const auto kern = rope_cache_kernel<T, VEC>;
+  if (!prefer_max_shared(reinterpret_cast<const void*>(kern))) return PSB_ERR_CUDA;
+  const int64_t units = static_cast<int64_t>(p.tokens) * (p.hq + 2 * p.hkv) * (p.head_dim / 2 / VEC);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, static_cast<int64_t>(sms) * 8));
+  discard_stale_error();
+  const cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, p);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  return check_launch();
+}
+
+bool aligned16(const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
+
+}  // namespace
+}  // namespace psb
+
+using namespace psb;
+
+extern "C" int psb_rope_reshape_and_cache(const void* query, int64_t q_stride_t, int64_t q_stride_h, void* query_out,
+                                          int64_t qo_stride_t, int64_t qo_stride_h, const void* key,
+                                          int64_t k_stride_t, int64_t k_stride_h, void* key_out, int64_t ko_stride_t,
+                                          int64_t ko_stride_h, const void* value, int64_t v_stride_t,
+                                          int64_t v_stride_h, const void* cos, const void* sin,
+                                          int64_t cs_stride_t, void* k_cache, void* v_cache,
+                                          const int64_t* slot_mapping, int32_t num_tokens, int32_t num_q_heads,
+                                          int32_t layer, int32_t num_layers, int64_t num_blocks,
+                                          int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype,
+                                          int32_t* error_flag, psb_stream_t stream) {
+  if (num_tokens < 0 || num_q_heads < 0 || num_layers <= 0 || layer < 0 || layer >= num_layers ||
+      num_blocks <= 0 || num_kv_heads <= 0 || block_size <= 0 || head_dim <= 0 || head_dim % 2)
+    return PSB_ERR_INVALID;
+  if (dtype != PSB_F32 && dtype != PSB_F16 && dtype != PSB_BF16) return PSB_ERR_INVALID;
+  if (num_tokens == 0) return PSB_OK;
+  if (!key || !value || !cos || !sin || !k_cache || !v_cache || !slot_mapping) return PSB_ERR_INVALID;
+  if (num_q_heads > 0 && (!query || !query_out)) return PSB_ERR_INVALID;
+  const int esz = elem_bytes(dtype);
+  RopeParams p;
+  p.q = static_cast<const char*>(query);
+  p.qst = q_stride_t * esz;
+  p.qsh = q_stride_h * esz;
+  p.qo = static_cast<char*>(query_out);
+  p.qost = qo_stride_t * esz;
+  p.qosh = qo_stride_h * esz;
+  p.k = static_cast<const char*>(key);
+  p.kst = k_stride_t * esz;
+  p.ksh = k_stride_h * esz;
+  p.ko = static_cast<char*>(key_out);
+  p.kost = ko_stride_t * esz;
+  p.kosh = ko_stride_h * esz;
+  p.v = static_cast<const char*>(value);
+  p.vst = v_stride_t * esz;
+  p.vsh = v_stride_h * esz;
+  p.cos = static_cast<const char*>(cos);
+  p.sin = static_cast<const char*>(sin);
+  p.cst = cs_stride_t * esz;
+  p.kc = static_cast<char*>(k_cache);
+  p.vc = static_cast<char*>(v_cache);
+  p.slots = slot_mapping;
+  p.tokens = num_tokens;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.block_size = block_size;
+  p.head_dim = head_dim;
+  p.layer_base_tiles = static_cast<int64_t>(layer) * num_blocks * num_kv_heads;
+  p.pool_slots = num_blocks * block_size;
+  p.err = error_flag;
+  const int sms = device_sm_count();
+  if (sms <= 0) return PSB_ERR_CUDA;
+  // 16-byte pieces when every row, stride and half-row is 16-byte aligned
+  const int64_t half_bytes = static_cast<int64_t>(head_dim / 2) * esz;
+  bool vec = half_bytes % 16 == 0 && aligned16(key) && aligned16(value) && aligned16(cos) && aligned16(sin) &&
+             aligned16(k_cache) && aligned16(v_cache) && p.kst % 16 == 0 && p.ksh % 16 == 0 && p.vst % 16 == 0 &&
+             p.vsh % 16 == 0 && p.cst % 16 == 0;
+  if (num_q_heads > 0)
+    vec = vec && aligned16(query) && aligned16(query_out) && p.qst % 16 == 0 && p.qsh % 16 == 0 &&
+          p.qost % 16 == 0 && p.qosh % 16 == 0;
+  if (key_out != nullptr) vec = vec && aligned16(key_out) && p.kost % 16 == 0 && p.kosh % 16 == 0;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PSB_BF16: return vec ? launch_rope<__nv_bfloat16, 8>(p, s, sms) : launch_rope<__nv_bfloat16, 1>(p, s, sms);
+    case PSB_F16: return vec ? launch_rope<__half, 8>(p, s, sms) : launch_rope<__half, 1>(p, s, sms);
+    default: return vec ? launch_rope<float, 4>(p, s, sms) : launch_rope<float, 1>(p, s, sms);
+  }
+}

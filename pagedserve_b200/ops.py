@@ -85,6 +85,65 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
         dtype_code(k_cache.dtype), _ptr(error_flag), _stream(key.device)), "reshape_and_cache")
 
 
+def rope_reshape_and_cache(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, cos: torch.Tensor,
+                           sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                           layer: int, query_out: torch.Tensor | None = None,
+                           key_out: torch.Tensor | None | bool = None,
+                           error_flag: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Rotary embedding of ``query [T, Hq, D]`` and ``key [T, Hkv, D]`` with
+    the per-token ``cos, sin [T, D]`` rows, fused with the slot-mapped write
+    of the rotated keys and of ``value`` into ``k_cache/v_cache[layer]``
+    (psb_rope_reshape_and_cache; bit-exact with the reference's
+    ``apply_rotary_pos_emb`` then ``write_token``).
+
+    Returns ``(query_out, key_out)``: ``query_out`` defaults to a new tensor
+    (pass ``query`` to rotate in place); ``key_out`` defaults to a new tensor
+    holding the rotated keys, ``False`` skips it (the pool still gets them).
+    """
+    _require_cuda(query, key, value, cos, sin, k_cache, v_cache, slot_mapping)
+    nl, nb, hkv, bs, d = _pool_geometry(k_cache, v_cache)
+    if query.ndim != 3 or query.shape[2] != d:
+        raise ValueError(f"query must be [T, Hq, {d}]")
+    t = query.shape[0]
+    if key.shape != (t, hkv, d) or value.shape != (t, hkv, d):
+        raise ValueError(f"key/value must be [{t}, {hkv}, {d}]")
+    cos = cos.reshape(-1, d)
+    sin = sin.reshape(-1, d)
+    if cos.shape[0] != t or sin.shape != cos.shape:
+        raise ValueError(f"cos/sin must hold one [{d}] row per token")
+    if cos.stride(1) != 1 or sin.stride(1) != 1 or cos.stride(0) != sin.stride(0):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    for x in (query, key, value, cos, sin):
+        if x.dtype != k_cache.dtype:
+            raise ValueError("query/key/value/cos/sin dtype must match the cache dtype")
+        if x.stride(-1) != 1:
+            raise ValueError("unit stride along head_dim is required")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (t,):
+        raise ValueError("slot_mapping must be int64 [T]")
+    slot_mapping = slot_mapping.contiguous()
+    if not 0 <= layer < nl:
+        raise ValueError("Invalid layer")
+    if query_out is None:
+        query_out = torch.empty_like(query)
+    if query_out.shape != query.shape or query_out.dtype != query.dtype or query_out.stride(2) != 1:
+        raise ValueError("query_out must match query's shape and dtype with unit stride along head_dim")
+    if key_out is None:
+        key_out = torch.empty_like(key)
+    elif key_out is False:
+        key_out = None
+    if key_out is not None and (key_out.shape != key.shape or key_out.dtype != key.dtype or key_out.stride(2) != 1):
+        raise ValueError("key_out must match key's shape and dtype with unit stride along head_dim")
+    lib = _native.load()
+    _native.check(lib.psb_rope_reshape_and_cache(
+        query.data_ptr(), query.stride(0), query.stride(1), query_out.data_ptr(), query_out.stride(0),
+        query_out.stride(1), key.data_ptr(), key.stride(0), key.stride(1), _ptr(key_out),
+        key_out.stride(0) if key_out is not None else 0, key_out.stride(1) if key_out is not None else 0,
+        value.data_ptr(), value.stride(0), value.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+        k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(), t, query.shape[1], layer, nl, nb, hkv, bs, d,
+        dtype_code(k_cache.dtype), _ptr(error_flag), _stream(query.device)), "rope_reshape_and_cache")
+    return query_out, key_out
+
+
 class DecodeWorkspace:
     """Split-K scratch for ``paged_decode``: one growable buffer per device.
 
