@@ -123,10 +123,21 @@ def prefill_flops(lens) -> float:
     return float(sum(4 * HQ * D * n * (n + 1) / 2 for n in lens))
 
 
+def rope_cache_bytes(n_tokens: int) -> int:
+    """Algorithmic bytes of rope_reshape_and_cache per token: read q, k, v, the
+    cos and sin rows and the slot; write the rotated q and k and the pool's
+    k and v rows (2568 + 2560 B for 14q/2kv heads, D 64, bf16)."""
+    row = D * 2
+    reads = (HQ + 2 * HKV) * row + 2 * row + 8
+    writes = (HQ + HKV) * row + 2 * HKV * row
+    return n_tokens * (reads + writes)
+
+
 def run_prefill(args, device, seed: int) -> dict:
-    """Packed causal prefill with the paged KV write of one engine iteration
-    (varlen_prefill + reshape_and_cache of every prompt token), on PREFILL_PACKS
-    different packs in turn so consecutive steps do not run from L2."""
+    """Packed causal prefill of one engine iteration: the fused RoPE + paged KV
+    write of every prompt token (rope_reshape_and_cache), then varlen_prefill
+    over the rotated q and k, on PREFILL_PACKS different packs in turn so
+    consecutive steps do not run from L2."""
     from pagedserve_b200 import ops
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
@@ -144,7 +155,15 @@ def run_prefill(args, device, seed: int) -> dict:
             at += k
             pos = torch.arange(n)
             slots.append(blocks[pos // BS] * BS + pos % BS)
+        # the engine's position embeddings: Qwen2 rope (theta 1e6) angles in
+        # fp32, cos/sin rounded to the model dtype, one row per token
+        pos = torch.cat([torch.arange(n) for n in lens]).to(device=device, dtype=torch.float32)
+        inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
+        ang = torch.outer(pos, inv).repeat(1, 2)
         packs.append(dict(
+            cos=ang.cos().to(torch.bfloat16), sin=ang.sin().to(torch.bfloat16),
+            q_rot=torch.empty(t, HQ, D, device=device, dtype=torch.bfloat16),
+            k_rot=torch.empty(t, HKV, D, device=device, dtype=torch.bfloat16),
             lens=lens, q=torch.randn(t, HQ, D, device=device, dtype=torch.bfloat16, generator=gen),
             k=torch.randn(t, HKV, D, device=device, dtype=torch.bfloat16, generator=gen),
             v=torch.randn(t, HKV, D, device=device, dtype=torch.bfloat16, generator=gen),
@@ -156,18 +175,19 @@ def run_prefill(args, device, seed: int) -> dict:
 
     def step(pk, attn=True, write=True):
         if write:
-            ops.reshape_and_cache(pk["k"], pk["v"], pk["kc"], pk["vc"], pk["slots"], 0)
+            ops.rope_reshape_and_cache(pk["q"], pk["k"], pk["v"], pk["cos"], pk["sin"], pk["kc"], pk["vc"],
+                                       pk["slots"], 0, query_out=pk["q_rot"], key_out=pk["k_rot"])
         if attn:
-            ops.varlen_prefill(pk["q"], pk["k"], pk["v"], pk["cu"], max(pk["lens"]), out=pk["out"])
+            ops.varlen_prefill(pk["q_rot"], pk["k_rot"], pk["v"], pk["cu"], max(pk["lens"]), out=pk["out"])
 
     stream = torch.cuda.Stream(device)
-    graphs, attn_graphs = [], []
+    graphs, attn_graphs, rope_graphs = [], [], []
     with torch.cuda.stream(stream):
         for pk in packs:
             step(pk)
         torch.cuda.synchronize()
         for pk in packs:
-            for lst, kw in ((graphs, {}), (attn_graphs, {"write": False})):
+            for lst, kw in ((graphs, {}), (attn_graphs, {"write": False}), (rope_graphs, {"attn": False})):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
                     step(pk, **kw)
@@ -186,22 +206,29 @@ def run_prefill(args, device, seed: int) -> dict:
         torch.cuda.synchronize()
         return a.elapsed_time(b) / args.steps
 
-    step_ms, attn_ms = timed(graphs), timed(attn_graphs)
-    for g in graphs + attn_graphs:
+    step_ms, attn_ms, rope_ms = timed(graphs), timed(attn_graphs), timed(rope_graphs)
+    for g in graphs + attn_graphs + rope_graphs:
         g.reset()
     flops = statistics.mean(prefill_flops(pk["lens"]) for pk in packs)
     tokens = statistics.mean(sum(pk["lens"]) for pk in packs)
     peak, kind = load_tensor_peak()
     tflops = flops / (attn_ms * 1e-3) / 1e12
+    rope_bytes = statistics.mean(rope_cache_bytes(sum(pk["lens"])) for pk in packs)
+    hbm_peak, hbm_kind = load_peaks()
+    rope_gbs = rope_bytes / (rope_ms * 1e-3) / 1e9
     return {
-        "workload": "packed causal prefill + paged KV write: prompts lognormal(median 256, sigma 1.0) clipped "
-                    "[32, 2048], packed to <= 16384 tokens, 14q/2kv heads, d64, block 16, bf16; "
-                    f"{PREFILL_PACKS} packs in turn",
+        "workload": "packed causal prefill + fused RoPE and paged KV write: prompts lognormal(median 256, sigma "
+                    "1.0) clipped [32, 2048], packed to <= 16384 tokens, 14q/2kv heads, d64, block 16, bf16, "
+                    f"rope theta 1e6; {PREFILL_PACKS} packs in turn",
         "seqs_per_pack": [len(pk["lens"]) for pk in packs], "tokens_per_pack": tokens,
         "ms_per_step": round(step_ms, 5), "attn_layer_tokens_per_s": round(tokens / (step_ms * 1e-3), 1),
         "attention": {"kernel": "prefill_tc_kernel (tcgen05/TMEM, TMA)", "ms": round(attn_ms, 5),
                       "gflop": round(flops / 1e9, 3), "tflops": round(tflops, 1), "peak_tflops": peak,
                       "peak_kind": kind, "frac": round(tflops / peak, 4), "bound": "tensor"},
+        "rope_cache": {"kernel": "rope_cache_kernel (RoPE of q and k + slot-mapped K/V write)",
+                       "ms": round(rope_ms, 5), "mbytes": round(rope_bytes / 1e6, 2),
+                       "gbs": round(rope_gbs, 1), "peak_gbs": hbm_peak, "peak_kind": hbm_kind,
+                       "frac": round(rope_gbs / hbm_peak, 4), "bound": "hbm"},
         "gpu_launches_per_step": 2,
     }
 
