@@ -236,6 +236,32 @@ int psb_varlen_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, co
                        int32_t head_dim, int32_t dtype, float scale, int32_t* error_flag, psb_stream_t stream);
 
 /*
+ * paged_prefill: prefix-aware (chunked) causal prefill over the paged pool.
+ *
+ * The reference's paged_attention(query [Hq, S, D], cache, request_id, layer,
+ * query_start_position) (pagedserve/attention/paged_attention.py:10-146), for
+ * a packed batch: q [total_tokens, q_heads, head_dim] holds each sequence's
+ * new rows, sequence i owning rows cu_seqlens[i] .. cu_seqlens[i+1] (n_i of
+ * them); the sequence has context_lens[i] tokens in the pool, read through
+ * block_tables[i, :], its query rows being the last n_i of them (their K/V
+ * already written).  Row j attends to positions 0 .. context_lens[i] - n_i + j
+ * (GQA, fp32 softmax, probabilities rounded to the input type before P.V).
+ * With context_lens == n the result equals psb_varlen_prefill on the same
+ * keys.  bf16/f16 with head_dim 64 and block_size 16 run the tcgen05 kernel
+ * (pool tiles loaded by TMA through the table); other geometries a CUDA-core
+ * kernel.  A context shorter than its query rows or longer than max_context,
+ * and block ids outside the pool, are flagged (PSB_DEVERR_CONTEXT /
+ * PSB_DEVERR_BLOCK_RANGE) instead of read.
+ */
+int psb_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k_cache,
+                      const void* v_cache, const int32_t* block_tables, int64_t table_stride,
+                      const int32_t* context_lens, void* out, int64_t o_stride_t, int64_t o_stride_h,
+                      const int32_t* cu_seqlens, int32_t num_seqs, int32_t total_tokens, int32_t max_seqlen,
+                      int32_t max_context, int32_t q_heads, int32_t layer, int32_t num_layers, int64_t num_blocks,
+                      int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype, float scale,
+                      int32_t* error_flag, psb_stream_t stream);
+
+/*
  * pack_step: GPU-side ragged-batch packer for one engine step.
  *
  * Inputs (device): for each of ``batch`` scheduled requests, ``req_rows[b]``

@@ -46,6 +46,9 @@ SIGNATURES = {
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64,
         _i64, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32, _i64, _i32, _i32,
         _i32, _i32, _c_void_p, _c_void_p]),
+    "psb_paged_prefill": (ctypes.c_int, [
+        _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _c_void_p,
+        _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _f32, _c_void_p, _c_void_p]),
     "psb_paged_decode_append": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64,
         _i64, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32,

@@ -176,6 +176,27 @@ bool encode_rows_map(CUtensorMap* map, const void* base, int64_t rows, int heads
   return true;
 }
 
+bool encode_pool_map(CUtensorMap* map, const void* base, int64_t tiles, int block_size, int head_dim,
+                     CUtensorMapDataType dt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const size_t esz = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(block_size),
+                              static_cast<cuuint64_t>(tiles)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * esz),
+                                 static_cast<cuuint64_t>(block_size) * head_dim * esz};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(head_dim), static_cast<cuuint32_t>(block_size), 1u};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = 10000 + static_cast<int>(r);
+    return false;
+  }
+  return true;
+}
+
 }  // namespace psb
 
 extern "C" const char* psb_version(void) { return "pagedserve_b200 0.1.0 sm_100a"; }

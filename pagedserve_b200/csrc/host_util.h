@@ -71,6 +71,12 @@ bool encode_pool_tile_map(CUtensorMap* map, const void* pool, int64_t tiles, int
 bool encode_rows_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int head_dim, int64_t row_stride,
                      int64_t head_stride, int box_rows, CUtensorMapDataType dt);
 
+// 3D tensor map over a paged K or V pool [layers * blocks * kv heads tiles,
+// block_size rows, head_dim]: one box is one (layer, block, kv head) tile of
+// block_size x head_dim, 128-byte swizzled.
+bool encode_pool_map(CUtensorMap* map, const void* base, int64_t tiles, int block_size, int head_dim,
+                     CUtensorMapDataType dt);
+
 // 2-D tiled map over a row-major [rows, cols] matrix with row pitch
 // ``row_stride_elems``; box = box_rows x box_cols, 128-byte swizzle.
 bool encode_matrix_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,

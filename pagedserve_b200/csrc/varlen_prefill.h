@@ -16,6 +16,16 @@ struct PrefillParams {
   int32_t num_seqs, total, max_seqlen, hq, hkv, head_dim;
   float scale_log2;
   int32_t* err;
+  // paged prefill (psb_paged_prefill): k and v are the pools
+  // [num_layers, num_blocks, hkv, block_size, head_dim]; sequence i's keys are
+  // positions 0 .. ctx[i] - 1 read through tables[i, :], and its cu-rows are
+  // the last (cu[i+1] - cu[i]) of them
+  bool paged = false;
+  const int32_t* tables = nullptr;
+  int64_t table_stride = 0;
+  const int32_t* ctx = nullptr;
+  int32_t layer = 0, num_layers_total = 0, block_size = 0, max_context = 0;
+  int64_t num_blocks = 0;
 };
 
 // tcgen05 / TMEM kernel (varlen_prefill_tc.cu): bf16/f16, head_dim 64,

@@ -74,9 +74,16 @@ __device__ __forceinline__ int seq_len(const PrefillParams& p, int s) {
 
 struct TileInfo {
   int q0, len, qblk, head, kvh, n_kv;
+  int seq, start, ctx;  // query row i sits at position start + i of ctx keys
 };
 
-template <typename T>
+constexpr int kPoolBlock = 16;                      // paged: rows per pool block
+constexpr uint32_t kPoolTile = kPoolBlock * kDim * 2;  // bytes of one (block, kv head) tile
+
+// PAGED (psb_paged_prefill): K/V come from the pools through the block table,
+// four pool tiles per 64-key step, and a sequence's query rows are the last
+// positions of its context; otherwise from the packed k/v rows of the batch.
+template <typename T, bool PAGED>
 __global__ void __launch_bounds__(kTcThreads, 2)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
@@ -162,7 +169,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     ti.kvh = ti.head / group;
     ti.q0 = p.cu[seq];
     ti.len = seq_len(p, seq);
-    ti.n_kv = min(2 * (lo + 1), (ti.len + kBN - 1) / kBN);
+    ti.seq = seq;
+    ti.ctx = ti.len;
+    if constexpr (PAGED) {
+      int c = p.ctx[seq];  // at least the query rows, at most max_context (else flagged, clamped)
+      if (c < ti.len || c > p.max_context) {
+        flag_error(p.err, PSB_DEVERR_CONTEXT);
+        c = c < ti.len ? ti.len : p.max_context;
+      }
+      ti.ctx = c;
+    }
+    ti.start = ti.ctx - ti.len;
+    ti.n_kv = (ti.start + min(ti.len, (lo + 1) * kBM) + kBN - 1) / kBN;  // keys [0, start + last row + 1)
     return ti;
   };
   const uint32_t s_base = smem_u32(smem);
@@ -279,9 +297,38 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               continue;
             }
             const int st = rg % kKvStages;
-            mbar_arrive_expect_tx(bar_kv + st, 2 * kKvTile);
-            tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
-            tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+            if constexpr (PAGED) {
+              // the step's four pool blocks; blocks past the context are not
+              // loaded (the softmax zeroes their V rows), bad ids are flagged
+              const int nblk = (ti.ctx + kPoolBlock - 1) / kPoolBlock;
+              const int32_t* row = p.tables + static_cast<int64_t>(ti.seq) * p.table_stride;
+              int32_t ids[kBN / kPoolBlock];
+#pragma unroll
+              for (int b = 0; b < kBN / kPoolBlock; ++b) {
+                const int idx = rj * (kBN / kPoolBlock) + b;
+                ids[b] = idx < nblk ? __ldg(row + idx) : -1;
+                if (idx < nblk && (ids[b] < 0 || ids[b] >= p.num_blocks)) {
+                  flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
+                  ids[b] = -1;
+                }
+              }
+              uint32_t bytes = 0;
+#pragma unroll
+              for (int b = 0; b < kBN / kPoolBlock; ++b) bytes += ids[b] >= 0 ? 2 * kPoolTile : 0;
+              mbar_arrive_expect_tx(bar_kv + st, bytes);
+#pragma unroll
+              for (int b = 0; b < kBN / kPoolBlock; ++b) {
+                if (ids[b] < 0) continue;
+                const int32_t tile = static_cast<int32_t>((static_cast<int64_t>(p.layer) * p.num_blocks + ids[b]) *
+                                                          p.hkv + ti.kvh);
+                tma_load_3d(smem + kOffK + st * kKvTile + b * kPoolTile, &tm_k, 0, 0, tile, bar_kv + st);
+                tma_load_3d(smem + kOffV + st * kKvTile + b * kPoolTile, &tm_v, 0, 0, tile, bar_kv + st);
+              }
+            } else {
+              mbar_arrive_expect_tx(bar_kv + st, 2 * kKvTile);
+              tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+              tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+            }
             ++rj;
             ++rg;
           }
@@ -362,8 +409,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(bar_sfree + (g & 1));  // the S buffer may take step g + 2
-        // keys past this row's position or past the sequence only occur in the last steps
-        const int lim = min(qrow, ti.len - 1) - j * kBN;  // last valid key column
+        if (PAGED && j == ti.n_kv - 1 && row < kBN && j * kBN + row >= ti.ctx) {
+          // V rows past the context (stale or never loaded) must not reach
+          // P.V, where 0 * NaN would be NaN: zero them before this thread's
+          // arrival lets P.V read the stage (the Q.K^T just read, and it
+          // followed the stage's copies)
+          const uint32_t vrow = s_base + kOffV + (g % kKvStages) * kKvTile + row * 128;
+#pragma unroll
+          for (int c = 0; c < 128; c += 16) st_shared_zero16(vrow + c);
+          fence_proxy_async_smem();  // visible to the tensor core
+        }
+        // keys past this row's position or past the context only occur in the last steps
+        const int lim = min(ti.start + qrow, ti.ctx - 1) - j * kBN;  // last valid key column
         float mx = -INFINITY;
         if (lim >= kBN - 1) {
 #pragma unroll
@@ -477,10 +534,13 @@ size_t tc_smem_bytes(int max_level, int num_seqs) {
 
 bool prefill_tc_supported(const PrefillParams& p, int dtype) {
   if (!(dtype == PSB_BF16 || dtype == PSB_F16) || p.head_dim != kDim) return false;
+  if (p.paged && p.block_size != kPoolBlock) return false;
   auto al16 = [](const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; };
-  // TMA: 16-byte aligned bases and strides; 4-byte output pairs
-  const bool strides = p.qst % 8 == 0 && p.qsh % 8 == 0 && p.kst % 8 == 0 && p.ksh % 8 == 0 && p.vst % 8 == 0 &&
-                       p.vsh % 8 == 0 && p.ost % 2 == 0 && p.osh % 2 == 0 && p.qst > 0 && p.kst > 0 && p.vst > 0;
+  // TMA: 16-byte aligned bases and strides (the pools are contiguous); 4-byte output pairs
+  const bool kv_strides = p.paged || (p.kst % 8 == 0 && p.ksh % 8 == 0 && p.vst % 8 == 0 && p.vsh % 8 == 0 &&
+                                      p.kst > 0 && p.vst > 0);
+  const bool strides = p.qst % 8 == 0 && p.qsh % 8 == 0 && kv_strides && p.ost % 2 == 0 && p.osh % 2 == 0 &&
+                       p.qst > 0;
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
   return strides && al16(p.q) && al16(p.k) && al16(p.v) && reinterpret_cast<uintptr_t>(p.out) % 4 == 0 &&
          max_level <= kMaxLevels && p.num_seqs <= kMaxTcSeqs && tc_smem_bytes(max_level, p.num_seqs) <= 227 * 1024;
@@ -489,18 +549,25 @@ bool prefill_tc_supported(const PrefillParams& p, int dtype) {
 int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
   const CUtensorMapDataType dt = dtype == PSB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
-  if (!encode_rows_map(&tq, p.q, p.total, p.hq, kDim, p.qst, p.qsh, kBM, dt) ||
-      !encode_rows_map(&tk, p.k, p.total, p.hkv, kDim, p.kst, p.ksh, kBN, dt) ||
-      !encode_rows_map(&tv, p.v, p.total, p.hkv, kDim, p.vst, p.vsh, kBN, dt))
+  if (!encode_rows_map(&tq, p.q, p.total, p.hq, kDim, p.qst, p.qsh, kBM, dt)) return PSB_ERR_CUDA;
+  if (p.paged) {
+    // the pools as (layer, block, kv head) tiles of 16 x 64
+    const int64_t tiles = static_cast<int64_t>(p.num_layers_total) * p.num_blocks * p.hkv;
+    if (!encode_pool_map(&tk, p.k, tiles, kPoolBlock, kDim, dt) || !encode_pool_map(&tv, p.v, tiles, kPoolBlock, kDim, dt))
+      return PSB_ERR_CUDA;
+  } else if (!encode_rows_map(&tk, p.k, p.total, p.hkv, kDim, p.kst, p.ksh, kBN, dt) ||
+             !encode_rows_map(&tv, p.v, p.total, p.hkv, kDim, p.vst, p.vsh, kBN, dt)) {
     return PSB_ERR_CUDA;
+  }
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
   // an upper bound of the tiles: sum over sequences of ceil(len / 128), times the heads
   const int64_t tiles = (static_cast<int64_t>(p.total) / kBM + p.num_seqs) * p.hq;
   if (tiles == 0) return PSB_OK;
   if (tiles >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
   const size_t smem = tc_smem_bytes(max_level, p.num_seqs);
-  const void* kern = dtype == PSB_BF16 ? reinterpret_cast<const void*>(prefill_tc_kernel<__nv_bfloat16>)
-                                       : reinterpret_cast<const void*>(prefill_tc_kernel<__half>);
+  const auto bf = p.paged ? prefill_tc_kernel<__nv_bfloat16, true> : prefill_tc_kernel<__nv_bfloat16, false>;
+  const auto hf = p.paged ? prefill_tc_kernel<__half, true> : prefill_tc_kernel<__half, false>;
+  const void* kern = dtype == PSB_BF16 ? reinterpret_cast<const void*>(bf) : reinterpret_cast<const void*>(hf);
   int occ = 0;
   if (!kernel_occupancy(kern, kTcThreads, smem, &occ) || occ < 1) return PSB_ERR_CUDA;
   const int sms = device_sm_count();
@@ -509,11 +576,9 @@ int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
   discard_stale_error();
   cudaError_t e;
   if (dtype == PSB_BF16)
-    e = launch_pdl(prefill_tc_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, s, p,
-                   tq, tk, tv);
+    e = launch_pdl(bf, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, s, p, tq, tk, tv);
   else
-    e = launch_pdl(prefill_tc_kernel<__half>, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, s, p, tq, tk,
-                   tv);
+    e = launch_pdl(hf, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, s, p, tq, tk, tv);
   if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }

@@ -290,6 +290,60 @@ def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens
     return out
 
 
+def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                  context_lens: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int, layer: int,
+                  scale: float | None = None, out: torch.Tensor | None = None, max_context: int | None = None,
+                  error_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """Prefix-aware (chunked) causal prefill over the paged pool.
+
+    ``q [T, Hq, D]`` packs each sequence's new rows (``cu_seqlens [B+1]``
+    int32); sequence ``b`` holds ``context_lens[b]`` tokens in the pool,
+    read through ``block_tables[b]``, its query rows being the last
+    ``cu_seqlens[b+1] - cu_seqlens[b]`` of them (their K/V already written,
+    e.g. by ``rope_reshape_and_cache``).  Row ``i`` of sequence ``b`` attends
+    to positions ``0 .. context_lens[b] - n_b + i``: the reference's
+    ``paged_attention(query, cache, request, layer, query_start_position)``
+    (pagedserve/attention/paged_attention.py:10-146) for a whole batch.
+    """
+    _require_cuda(q, k_cache, v_cache, block_tables, context_lens, cu_seqlens)
+    nl, nb, hkv, bs, d = _pool_geometry(k_cache, v_cache)
+    if q.ndim != 3 or q.shape[2] != d:
+        raise ValueError(f"q must be [T, Hq, {d}]")
+    t, hq, _ = q.shape
+    if hq % hkv:
+        raise ValueError("Query heads must be divisible by KV heads")
+    if q.dtype != k_cache.dtype:
+        raise ValueError("q dtype must match the cache dtype")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.ndim != 1 or cu_seqlens.shape[0] < 1:
+        raise ValueError("cu_seqlens must be int32 [B+1]")
+    batch = cu_seqlens.shape[0] - 1
+    if block_tables.dtype != torch.int32 or block_tables.ndim != 2 or block_tables.shape[0] != batch:
+        raise ValueError("block_tables must be int32 [B, max_blocks]")
+    if context_lens.dtype != torch.int32 or context_lens.shape != (batch,):
+        raise ValueError("context_lens must be int32 [B]")
+    if not 0 <= layer < nl:
+        raise ValueError("Invalid layer")
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    cu_seqlens, context_lens = cu_seqlens.contiguous(), context_lens.contiguous()
+    if max_context is None:
+        max_context = block_tables.shape[1] * bs
+    if out is None:
+        out = torch.empty_like(q)
+    if out.shape != q.shape or out.stride(2) != 1 or out.dtype != q.dtype:
+        raise ValueError("out must match q with unit stride along head_dim")
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    lib = _native.load()
+    _native.check(lib.psb_paged_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(),
+        block_tables.stride(0), context_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1),
+        cu_seqlens.data_ptr(), batch, t, int(max_seqlen), int(max_context), hq, layer, nl, nb, hkv, bs, d,
+        dtype_code(q.dtype), scale, _ptr(error_flag), _stream(q.device)), "paged_prefill")
+    return out
+
+
 def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.Tensor, query_lens: torch.Tensor,
               total: int, block_size: int, out_width: int | None = None, error_flag: torch.Tensor | None = None):
     """Build one step's ragged-batch metadata on the GPU.
