@@ -123,6 +123,12 @@ def prefill_flops(lens) -> float:
     return float(sum(4 * HQ * D * n * (n + 1) / 2 for n in lens))
 
 
+def chunk_flops(lens, chunks) -> float:
+    """FLOPs of prefilling the last ``c`` rows of an ``n``-token context: row
+    ``i`` of the chunk sees ``n - c + i + 1`` keys."""
+    return float(sum(4 * HQ * D * (c * (n - c) + c * (c + 1) / 2) for n, c in zip(lens, chunks)))
+
+
 def rope_cache_bytes(n_tokens: int) -> int:
     """Algorithmic bytes of rope_reshape_and_cache per token: read q, k, v, the
     cos and sin rows and the slot; write the rotated q and k and the pool's
@@ -149,18 +155,26 @@ def run_prefill(args, device, seed: int) -> dict:
         nb = int(math.ceil(SLACK * need))
         perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + i))[:need]
         slots, at = [], 0
-        for n in lens:
+        table = torch.zeros(len(lens), max(-(-n // BS) for n in lens), dtype=torch.int32)
+        for i, n in enumerate(lens):
             k = -(-n // BS)
             blocks = perm[at:at + k]
+            table[i, :k] = blocks.to(torch.int32)
             at += k
             pos = torch.arange(n)
             slots.append(blocks[pos // BS] * BS + pos % BS)
+        # chunked prefill: each prompt's second half attends over its first half
+        chunks = [n - n // 2 for n in lens]
+        rows = torch.cat([torch.arange(a + n // 2, a + n) for a, n in zip(np.cumsum([0] + lens[:-1]), lens)])
         # the engine's position embeddings: Qwen2 rope (theta 1e6) angles in
         # fp32, cos/sin rounded to the model dtype, one row per token
         pos = torch.cat([torch.arange(n) for n in lens]).to(device=device, dtype=torch.float32)
         inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device, dtype=torch.float32) / D))
         ang = torch.outer(pos, inv).repeat(1, 2)
         packs.append(dict(
+            table=table.to(device), ctx=torch.tensor(lens, dtype=torch.int32, device=device), chunks=chunks,
+            chunk_rows=rows.to(device), chunk_cu=torch.tensor([0] + list(np.cumsum(chunks)), dtype=torch.int32,
+                                                              device=device),
             cos=ang.cos().to(torch.bfloat16), sin=ang.sin().to(torch.bfloat16),
             q_rot=torch.empty(t, HQ, D, device=device, dtype=torch.bfloat16),
             k_rot=torch.empty(t, HKV, D, device=device, dtype=torch.bfloat16),
@@ -180,17 +194,29 @@ def run_prefill(args, device, seed: int) -> dict:
         if attn:
             ops.varlen_prefill(pk["q_rot"], pk["k_rot"], pk["v"], pk["cu"], max(pk["lens"]), out=pk["out"])
 
+    def paged(pk):  # the same prompts with K/V read from the pool through the tables
+        ops.paged_prefill(pk["q_rot"], pk["kc"], pk["vc"], pk["table"], pk["ctx"], pk["cu"], max(pk["lens"]), 0,
+                          out=pk["out"])
+
+    def chunked(pk):  # each prompt's second half over its first half, from the pool
+        ops.paged_prefill(pk["q_chunk"], pk["kc"], pk["vc"], pk["table"], pk["ctx"], pk["chunk_cu"],
+                          max(pk["chunks"]), 0, out=pk["out_chunk"])
+
     stream = torch.cuda.Stream(device)
-    graphs, attn_graphs, rope_graphs = [], [], []
+    graphs, attn_graphs, rope_graphs, paged_graphs, chunk_graphs = [], [], [], [], []
     with torch.cuda.stream(stream):
         for pk in packs:
             step(pk)
+            pk["q_chunk"] = pk["q_rot"].index_select(0, pk["chunk_rows"])
+            pk["out_chunk"] = torch.empty_like(pk["q_chunk"])
         torch.cuda.synchronize()
         for pk in packs:
-            for lst, kw in ((graphs, {}), (attn_graphs, {"write": False}), (rope_graphs, {"attn": False})):
+            for lst, fn in ((graphs, lambda: step(pk)), (attn_graphs, lambda: step(pk, write=False)),
+                            (rope_graphs, lambda: step(pk, attn=False)), (paged_graphs, lambda: paged(pk)),
+                            (chunk_graphs, lambda: chunked(pk))):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
-                    step(pk, **kw)
+                    fn()
                 lst.append(g)
     torch.cuda.synchronize()
 
@@ -207,7 +233,8 @@ def run_prefill(args, device, seed: int) -> dict:
         return a.elapsed_time(b) / args.steps
 
     step_ms, attn_ms, rope_ms = timed(graphs), timed(attn_graphs), timed(rope_graphs)
-    for g in graphs + attn_graphs + rope_graphs:
+    paged_ms, chunk_ms = timed(paged_graphs), timed(chunk_graphs)
+    for g in graphs + attn_graphs + rope_graphs + paged_graphs + chunk_graphs:
         g.reset()
     flops = statistics.mean(prefill_flops(pk["lens"]) for pk in packs)
     tokens = statistics.mean(sum(pk["lens"]) for pk in packs)
@@ -216,6 +243,8 @@ def run_prefill(args, device, seed: int) -> dict:
     rope_bytes = statistics.mean(rope_cache_bytes(sum(pk["lens"])) for pk in packs)
     hbm_peak, hbm_kind = load_peaks()
     rope_gbs = rope_bytes / (rope_ms * 1e-3) / 1e9
+    cflops = statistics.mean(chunk_flops(pk["lens"], pk["chunks"]) for pk in packs)
+    paged_tf, chunk_tf = flops / (paged_ms * 1e-3) / 1e12, cflops / (chunk_ms * 1e-3) / 1e12
     return {
         "workload": "packed causal prefill + fused RoPE and paged KV write: prompts lognormal(median 256, sigma "
                     "1.0) clipped [32, 2048], packed to <= 16384 tokens, 14q/2kv heads, d64, block 16, bf16, "
@@ -225,6 +254,12 @@ def run_prefill(args, device, seed: int) -> dict:
         "attention": {"kernel": "prefill_tc_kernel (tcgen05/TMEM, TMA)", "ms": round(attn_ms, 5),
                       "gflop": round(flops / 1e9, 3), "tflops": round(tflops, 1), "peak_tflops": peak,
                       "peak_kind": kind, "frac": round(tflops / peak, 4), "bound": "tensor"},
+        "paged_attention": {"kernel": "prefill_tc_kernel<paged> (K/V from the pool through the block tables)",
+                            "ms": round(paged_ms, 5), "tflops": round(paged_tf, 1), "frac": round(paged_tf / peak, 4)},
+        "chunked_attention": {"workload": "each prompt's second half prefilled over its first half (prefix read "
+                                          "from the pool)", "ms": round(chunk_ms, 5),
+                              "gflop": round(cflops / 1e9, 3), "tflops": round(chunk_tf, 1),
+                              "frac": round(chunk_tf / peak, 4)},
         "rope_cache": {"kernel": "rope_cache_kernel (RoPE of q and k + slot-mapped K/V write)",
                        "ms": round(rope_ms, 5), "mbytes": round(rope_bytes / 1e6, 2),
                        "gbs": round(rope_gbs, 1), "peak_gbs": hbm_peak, "peak_kind": hbm_kind,

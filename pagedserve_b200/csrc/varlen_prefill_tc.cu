@@ -286,6 +286,33 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (tn_valid) tn = tile_of(1);
         // K/V requests run ahead through the current and the next tile
         int rk = 0, rj = 0, rg = 0;  // tile (0 current, 1 next), step and global step of the next request
+        // paged: block ids of the request the cursor points at, loaded while
+        // the step before it runs (pf_g: its global step, -1 for none)
+        static_assert(kBN / kPoolBlock == 4, "four pool blocks per key step");
+        int4 pf_ids = make_int4(-1, -1, -1, -1);  // in registers: no local memory on the issue path
+        int pf_g = -1;
+        auto load_ids = [&](int seq, int ctx, int j) -> int4 {
+          const int nblk = (ctx + kPoolBlock - 1) / kPoolBlock;
+          const int32_t* row = p.tables + static_cast<int64_t>(seq) * p.table_stride + 4 * j;
+          const int n = nblk - 4 * j;
+          return make_int4(__ldg(row), n > 1 ? __ldg(row + 1) : -1, n > 2 ? __ldg(row + 2) : -1,
+                           n > 3 ? __ldg(row + 3) : -1);
+        };
+        auto prefetch_ids = [&]() {
+          if constexpr (PAGED) {
+            // the request the cursor points at: step rj of the current tile,
+            // or the first step of the next one
+            int seq = tc.seq, ctx = tc.ctx, j = rj;
+            if (rk == 1 || rj >= tc.n_kv) {
+              if (!tn_valid || (rk == 1 && rj >= tn.n_kv)) return;
+              seq = tn.seq;
+              ctx = tn.ctx;
+              j = rk == 1 ? rj : 0;
+            }
+            pf_ids = load_ids(seq, ctx, j);
+            pf_g = rg;
+          }
+        };
         auto request_kv = [&](int limit_g) {
           while (rg <= limit_g) {
             if (rk == 1 && !tn_valid) break;
@@ -301,12 +328,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               // the step's four pool blocks; blocks past the context are not
               // loaded (the softmax zeroes their V rows), bad ids are flagged
               const int nblk = (ti.ctx + kPoolBlock - 1) / kPoolBlock;
-              const int32_t* row = p.tables + static_cast<int64_t>(ti.seq) * p.table_stride;
-              int32_t ids[kBN / kPoolBlock];
+              const int4 id4 = pf_g == rg ? pf_ids : load_ids(ti.seq, ti.ctx, rj);
+              int32_t ids[kBN / kPoolBlock] = {id4.x, id4.y, id4.z, id4.w};
 #pragma unroll
               for (int b = 0; b < kBN / kPoolBlock; ++b) {
                 const int idx = rj * (kBN / kPoolBlock) + b;
-                ids[b] = idx < nblk ? __ldg(row + idx) : -1;
                 if (idx < nblk && (ids[b] < 0 || ids[b] >= p.num_blocks)) {
                   flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
                   ids[b] = -1;
@@ -338,6 +364,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         for (int k = 0; k < my_tiles && !fail; ++k) {
           const bool has_next = k + 1 < my_tiles;
           for (int j = 0; j < tc.n_kv && !fail; ++j, ++g) {
+            prefetch_ids();  // the next request's block ids land while this step runs
             // softmax step g done: P written (the next phase needs P.V of this
             // step, so the parity cannot alias)
             if (!mbar_wait(bar_p, g & 1)) {
