@@ -23,6 +23,12 @@ int device_sm_count();
 // them.
 bool prefer_max_shared(const void* func);
 
+// CTAs of ``func`` that fit on one SM at ``threads`` threads and ``smem``
+// dynamic shared bytes under the full carve-out: registers (per warp, in
+// units of 256), shared memory (plus static and the per-CTA reservation),
+// threads and CTA slots.
+int resident_ctas(const void* func, int threads, size_t smem);
+
 // Max resident CTAs per SM for ``func`` at ``threads`` and ``smem`` dynamic
 // bytes; raises the kernel's dynamic shared-memory limit when needed (and
 // sets the carve-out preference above).
