@@ -32,6 +32,9 @@
 //   producer: O += P V (four tcgen05.mma with P read from TMEM, N 64, V as an
 //   MN-major operand; the first step of a tile overwrites O, which the
 //   softmax warps have read for the previous tile before they got there).
+// P is double-buffered in TMEM: the softmax of step g waits only for the P.V
+// of step g - 2, and the producer issues P.V of step g before waiting for
+// step g - 1's, so the softmax and P.V of consecutive steps overlap.
 // Every mbarrier wait is bounded and each phase is waited for before the
 // barrier can move two phases on; on a timeout a CTA records
 // PSB_DEVERR_TIMEOUT, lets its copies and MMAs in flight land (bounded), frees
@@ -54,8 +57,8 @@ constexpr uint32_t kTile = kBM * kDim * 2;    // bytes of one Q tile (16 KB)
 constexpr uint32_t kKvTile = kBN * kDim * 2;  // bytes of one K or V tile (8 KB)
 constexpr int kKvStages = 4;                  // K/V ring depth
 constexpr int kKvAhead = kKvStages;           // K/V of step g + kKvAhead is requested once P.V of step g is done
-constexpr uint32_t kTmemCols = 256;  // S buffers: cols [0, 64), [64, 128); O: [128, 192); P: [192, 224)
-constexpr uint32_t kSCol = 0, kOCol = 128, kPCol = 192;
+constexpr uint32_t kTmemCols = 256;  // S buffers: cols [0, 64), [64, 128); O: [128, 192); P buffers: [192, 256)
+constexpr uint32_t kSCol = 0, kOCol = 128, kPCol = 192, kPCols = 32;
 constexpr float kRescaleLog2 = 8.f;  // rescale O when a row max grows by more than 2^8
 // dynamic shared memory (1024-byte aligned): Q0 | Q1 | K ring | V ring | barriers | tile tables
 constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 2 * kTile + kKvStages * kKvTile;
@@ -93,10 +96,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* bar_kv = bar_q + 2;                                      // [kKvStages]
   uint64_t* bar_s = bar_q + 2 + kKvStages;                           // [2]
   uint64_t* bar_sfree = bar_s + 2;  // [2] S buffer read by the softmax
-  uint64_t* bar_o = bar_sfree + 2;
-  uint64_t* bar_p = bar_o + 1;      // softmax step done: P written
-  uint64_t* bar_qfree = bar_p + 1;  // a tile's Q K^T done
+  uint64_t* bar_pv = bar_sfree + 2;  // [2] P.V of a step using P buffer g & 1 done
+  uint64_t* bar_p = bar_pv + 2;      // [2] softmax step done: P buffer g & 1 written
+  uint64_t* bar_qfree = bar_p + 2;   // a tile's Q K^T done
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_qfree + 1);
+  static_assert(15 * sizeof(uint64_t) + sizeof(uint32_t) <= kSmemBars, "barriers fit their area");
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
   int32_t* s_lstart = reinterpret_cast<int32_t*>(smem + kSmemTiles + kSmemBars);  // [max_level + 1]
   int32_t* s_cnt = s_lstart + (max_level + 1);   // [max_level + 1] sequences with more than i blocks
@@ -194,8 +198,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     mbar_init(bar_s + 1, 1);
     mbar_init(bar_sfree, kSoftmaxThreads);
     mbar_init(bar_sfree + 1, kSoftmaxThreads);
-    mbar_init(bar_o, 1);
+    mbar_init(bar_pv, 1);
+    mbar_init(bar_pv + 1, 1);
     mbar_init(bar_p, kSoftmaxThreads);
+    mbar_init(bar_p + 1, kSoftmaxThreads);
     mbar_init(bar_qfree, 1);
     fence_barrier_init();
   }
@@ -365,26 +371,30 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           const bool has_next = k + 1 < my_tiles;
           for (int j = 0; j < tc.n_kv && !fail; ++j, ++g) {
             prefetch_ids();  // the next request's block ids land while this step runs
-            // softmax step g done: P written (the next phase needs P.V of this
-            // step, so the parity cannot alias)
-            if (!mbar_wait(bar_p, g & 1)) {
+            // softmax step g done: P buffer g & 1 written (its next phase, step
+            // g + 2, needs P.V of this step first, so the parity cannot alias)
+            if (!mbar_wait(bar_p + (g & 1), (g >> 1) & 1)) {
               fail = true;
               break;
             }
             tc_fence_after();
             const uint64_t dvs = dv + static_cast<uint64_t>((g % kKvStages) * (kKvTile >> 4));
+            const uint32_t pcol = tmem + kPCol + (g & 1) * kPCols;
 #pragma unroll
             for (int kk = 0; kk < kBN / 16; ++kk)
-              umma_f16_ts(tmem + kOCol, tmem + kPCol + 8 * kk, dvs + 128 * kk, idesc_o, j > 0 || kk > 0);
-            umma_commit(bar_o);
+              umma_f16_ts(tmem + kOCol, pcol + 8 * kk, dvs + 128 * kk, idesc_o, j > 0 || kk > 0);
+            umma_commit(bar_pv + (g & 1));
             ++pv_issued;
-            // once this P.V is done its stage takes step g + kKvAhead
-            if (!mbar_wait(bar_o, g & 1)) {
-              fail = true;
-              break;
+            // the previous step's P.V (done in order before this one) frees its
+            // stage for step g - 1 + kKvAhead
+            if (g >= 1) {
+              if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) {
+                fail = true;
+                break;
+              }
+              ++pv_seen;
+              request_kv(g - 1 + kKvAhead);
             }
-            ++pv_seen;
-            request_kv(g + kKvAhead);
           }
           if (fail) break;
           if (has_next) {  // the next tile becomes current
@@ -397,14 +407,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             }
             tn_valid = k + 2 < my_tiles;
             if (tn_valid) tn = tile_of(k + 2);
-            // the new next tile may take requests now (P.V of step g - 1 was the last seen)
-            request_kv(g - 1 + kKvAhead);
+            // the new next tile may take requests now (P.V of step g - 2 was the last seen)
+            request_kv(g - 2 + kKvAhead);
           }
         }
         if (fail) {
           flag_error(p.err, PSB_DEVERR_TIMEOUT);
           // let copies and MMAs still in flight land before shared memory and TMEM are released
-          for (int t = pv_seen; t < pv_issued; ++t) (void)mbar_wait(bar_o, t & 1);
+          for (int t = pv_seen; t < pv_issued; ++t) (void)mbar_wait(bar_pv + (t & 1), (t >> 1) & 1);
           for (int t = 0; t < kKvStages && t < rg; ++t) {
             const int last = rg - 1 - ((rg - 1 - t) % kKvStages);  // the newest request of stage t
             (void)mbar_wait(bar_kv + t, (last / kKvStages) & 1);
@@ -467,7 +477,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           const float ms_new = grow ? mxs : ms;
           const float alpha = ms == -INFINITY ? 0.f : ex2_approx(ms - ms_new);  // 1 where the max stays
           if (j > 0) {  // O holds P.V of the earlier steps once the last of them is done
-            if (!mbar_wait(bar_o, (g - 1) & 1)) {
+            if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) {
               fail = true;
               break;
             }
@@ -496,24 +506,24 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           pk[c / 2] = pack2<T>(x0, x1);
         }
         l_run += rs;
-        // P overwrites the previous step's P in TMEM: wait for that P.V (issued
-        // right after the previous step, so normally long done; the next P.V
-        // cannot start before this thread's arrival below, so the parity cannot alias)
-        if (g > 0) {
-          if (!mbar_wait(bar_o, (g - 1) & 1)) {
+        // P buffer g & 1 held P of step g - 2: wait for that P.V (normally long
+        // done; P.V of step g cannot start before this thread's arrival below,
+        // so the parity cannot alias)
+        if (g >= 2) {
+          if (!mbar_wait(bar_pv + (g & 1), ((g - 2) >> 1) & 1)) {
             fail = true;
             break;
           }
         }
-        tmem_st32(t_lane + kPCol, pk);
+        tmem_st32(t_lane + kPCol + (g & 1) * kPCols, pk);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar_p);
+        mbar_arrive(bar_p + (g & 1));
       }
       if (fail) break;
       // the tile's last P.V, then its output (before this thread's arrival for
       // the next tile's first step lets the producer overwrite O)
-      if (!mbar_wait(bar_o, (g - 1) & 1)) {
+      if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) {
         fail = true;
         break;
       }
