@@ -6,7 +6,7 @@
 //
 // Fast path (bf16/f16, head_dim 64, block_size 16, up to 8 q heads per kv
 // head, or 16 with an odd kv-head count): the pool blocks of all sequences
-// are split evenly over the warps of a persistent grid (one CTA of 6 warps
+// are split evenly over the warps of a persistent grid (one CTA of 8 warps
 // per SM).  Each warp streams its blocks through a private shared-memory ring
 // with 16-byte cp.async copies, runs QK^T and PV on mma.sync m16n8k16 with
 // fp32 accumulation (all q heads of two kv heads packed into the 16 tile
@@ -288,7 +288,11 @@ __device__ void finish_unit(const DecodeParams& p, const Unit& w, int64_t u, con
 // Each warp is an independent stream with its own shared-memory ring of
 // kRing slots (K and V of one block of HP packed kv heads, plus the q rows
 // with a segment's first block), filled by 16-byte cp.async copies, one
-// commit group per block.  No CTA-wide barrier follows the prologue.
+// commit group per block.  No CTA-wide barrier follows the prologue.  Eight
+// warps of two slots each (two warps per SM sub-partition, 16 blocks in
+// flight per SM) measured faster than six of three (where warps 2 and 3 have a
+// sub-partition to themselves and outrun the rest by ~7 %) and than four of
+// four or five.
 //
 // Row packing.  The 16 rows of the m16n8k16 tile hold the q heads of HP kv
 // heads: with HP = 2 rows 0-7 are the (<= 8) q heads of kv head 2p and rows
@@ -296,9 +300,9 @@ __device__ void finish_unit(const DecodeParams& p, const Unit& w, int64_t u, con
 // tiles (adjacent in the pool) and every accumulator register carries a real
 // output; with HP = 1 the 16 rows are up to 16 q heads of one kv head.  Each
 // K/V byte leaves HBM exactly once.
-constexpr int kFastWarps = 6;
+constexpr int kFastWarps = 8;
 constexpr int kFastThreads = kFastWarps * 32;
-constexpr int kRing = 3;              // slots per warp
+constexpr int kRing = 2;              // slots per warp
 constexpr int kFastMinBlocks = 8;     // blocks per warp below which the grid shrinks
 constexpr int kMaxFastCtas = 160;     // grid limit (one CTA per SM; B200 has 148)
 
@@ -421,6 +425,19 @@ __device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void* src, u
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// Wait until the oldest of ``inflight`` (1 .. N) committed groups is complete.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_oldest(uint32_t inflight) {
+  if constexpr (N > 1) {
+    if (inflight >= N) {
+      cp_async_wait<N - 1>();
+      return;
+    }
+    cp_async_wait_oldest<N - 1>(inflight);
+  } else {
+    cp_async_wait<0>();
+  }
+}
 
 // APPEND: psb_paged_decode_append (the new-token store below); a separate
 // instantiation so plain decode carries none of it.
@@ -620,7 +637,6 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
   int32_t cseg = 0, cslot = 0;
   bool cfull = false;  // the current segment began at its sequence's first block
-  static_assert(kRing == 3, "the wait below assumes a three-slot ring");
   while (consumed != issued) {
     const uint32_t slot = consumed % kRing;
     const int32_t mt = __shfl_sync(0xffffffffu, meta, slot);
@@ -633,7 +649,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) decode_fast_kernel(const Deco
     }
     // the oldest copy group is complete once at most the newer ones are pending
     const uint32_t inflight = issued - consumed;
-    if (inflight >= 3) cp_async_wait<2>(); else if (inflight == 2) cp_async_wait<1>(); else cp_async_wait<0>();
+    cp_async_wait_oldest<kRing>(inflight);
     __syncwarp();  // every lane's copies are visible to every lane
     const uint32_t sbase = smem_u32(ring + slot * Geo::kSlot);
     if (APPEND && valid && ((mt >> 9) & 1)) {  // uniform over the warp
