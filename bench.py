@@ -52,7 +52,7 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 # DRAM bytes of one fused decode step (decode with the new-token store + combine)
 # on the rank-0 workload, measured with ncu
-STEP_TRAFFIC_BYTES = 196_300_000
+STEP_TRAFFIC_BYTES = 197_900_000
 
 
 def context_lengths(seed: int, n: int = BATCH) -> np.ndarray:
@@ -629,7 +629,7 @@ def run_b200(args, world, rank, local):
                          "bytes_per_launch": step_bytes,
                          "avg_launch_ms": round(rank_step_ms, 5), "traffic": STEP_TRAFFIC_BYTES,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused decode "
-                                           "(187.5 + 4.0 MB) and one combine (4.8 MB) launch on this seeded "
+                                           "(187.5 + 4.3 MB) and one combine (6.0 MB) launch on this seeded "
                                            "workload (decode ncu summary under profiles/)",
                          "decode_only_ms": round(dec_ms, 5),
                          "decode_only_note": "decode + combine without the new-token store, same graphs"},
