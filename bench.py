@@ -268,6 +268,89 @@ def run_prefill(args, device, seed: int) -> dict:
     }
 
 
+VOCAB = 151936        # Qwen2.5-0.5B vocabulary (tied embeddings)
+SELECT_BATCHES = (128, 256)  # greedy-sampling serving batch; this bench's decode batch
+SELECT_LAUNCHES = 8   # launches per captured graph, rotating over buffers larger than L2 together
+
+
+def run_select(args, device, seed: int) -> dict:
+    """Greedy selection of a decode step (select_tokens: argmax over the
+    vocabulary + EOS / remaining-token stop test) for the serving batches,
+    bf16 logits.  Each timed graph rotates over enough logits buffers that
+    together exceed the L2, so every launch streams its rows from HBM."""
+    from pagedserve_b200 import ops
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    eos = torch.tensor([151643, 151645], dtype=torch.int64, device=device)
+    hbm_peak, hbm_kind = load_peaks()
+    out = {"kernel": "select_stream_kernel (persistent thread-block clusters, bulk async copies into per-warp "
+                     "shared-memory slots, DSMEM merge)",
+           "workload": f"bf16 logits [B, {VOCAB}], EOS ids {{151643, 151645}}, remaining counters; buffers rotated "
+                       "so each graph's launches read > 126 MB", "batches": {}}
+    for batch in SELECT_BATCHES:
+        row_bytes = VOCAB * 2
+        nbuf = max(2, -(-200_000_000 // (batch * row_bytes)))
+        bufs = [torch.randn(batch, VOCAB, device=device, generator=gen).to(torch.bfloat16) for _ in range(nbuf)]
+        rem = torch.full((batch,), 1 << 30, dtype=torch.int32, device=device)
+        tokens = torch.empty(batch, dtype=torch.int64, device=device)
+        status = torch.empty(batch, dtype=torch.uint8, device=device)
+        nbytes = batch * row_bytes + batch * (8 + 1 + 2 * 4) + eos.numel() * 8
+        res = {"mbytes_per_launch": round(nbytes / 1e6, 3)}
+        stream = torch.cuda.Stream(device)
+        for ctas in (0, 1, 2, 4, 6, 8):
+            with torch.cuda.stream(stream):
+                ops.select_tokens(bufs[0], eos, rem, tokens=tokens, status=status, ctas_per_row=ctas)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(SELECT_LAUNCHES):
+                        ops.select_tokens(bufs[i % nbuf], eos, rem, tokens=tokens, status=status,
+                                          ctas_per_row=ctas)
+            for _ in range(args.warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            reps = max(1, args.steps // SELECT_LAUNCHES)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                g.replay()
+            e.record()
+            torch.cuda.synchronize()
+            g.reset()
+            ms = a.elapsed_time(e) / (reps * SELECT_LAUNCHES)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            res["auto" if ctas == 0 else f"ctas{ctas}"] = {"us": round(ms * 1e3, 3), "gbs": round(gbs, 1),
+                                                           "frac": round(gbs / hbm_peak, 4)}
+        # the reference's own expression, logits.argmax(dim=-1), on the same buffers
+        with torch.cuda.stream(stream):
+            torch.argmax(bufs[0], dim=-1, out=tokens)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(SELECT_LAUNCHES):
+                    torch.argmax(bufs[i % nbuf], dim=-1, out=tokens)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = max(1, args.steps // SELECT_LAUNCHES)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        g.reset()
+        res["torch_argmax_us"] = round(a.elapsed_time(e) / (reps * SELECT_LAUNCHES) * 1e3, 3)
+        # correctness of the timed configuration against torch on the last buffer
+        rem.fill_(1 << 30)
+        ops.select_tokens(bufs[-1], eos, rem, tokens=tokens, status=status)
+        res["matches_torch_argmax"] = bool(torch.equal(tokens, bufs[-1].argmax(dim=-1)))
+        out["batches"][str(batch)] = res
+        del bufs
+    out.update({"peak_gbs": hbm_peak, "peak_kind": hbm_kind, "bound": "hbm"})
+    return out
+
+
 # ---------------------------------------------------------------------------
 # distributed plumbing
 # ---------------------------------------------------------------------------
@@ -578,6 +661,7 @@ def run_b200(args, world, rank, local):
 
     # ---- packed prefill (one engine iteration's attention and KV write) ------
     prefill = run_prefill(args, device, 2000 + rank)
+    select = run_select(args, device, 3000 + rank)
 
     # ---- reduce over ranks: times by max, work by sum ------------------------
     from pagedserve_b200.sharding import aggregate_counters
@@ -643,6 +727,7 @@ def run_b200(args, world, rank, local):
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
             "clocks": clocks.summary(),
             "prefill": prefill,
+            "select_tokens": select,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu

@@ -48,7 +48,15 @@ enum {
   PSB_DEVERR_CONTEXT = 4,       /* context length > table width * block_size, or < 0 */
   PSB_DEVERR_WORKSPACE = 8,     /* split-K work exceeded the workspace */
   PSB_DEVERR_TIMEOUT = 16,      /* an async copy / MMA wait exceeded its bound */
-  PSB_DEVERR_SEQLENS = 32       /* cu_seqlens not non-decreasing within [0, total] */
+  PSB_DEVERR_SEQLENS = 32,      /* cu_seqlens not non-decreasing within [0, total] */
+  PSB_DEVERR_LIMIT = 64         /* psb_select_tokens: a row had no tokens left to generate */
+};
+
+/* per-row status bits written by psb_select_tokens */
+enum {
+  PSB_SELECT_DONE = 1,  /* the request finishes with this token (EOS, or its last allowed token) */
+  PSB_SELECT_EOS = 2,   /* the token is one of the EOS ids */
+  PSB_SELECT_LIMIT = 4  /* the row had no tokens left on entry: nothing was counted (flagged) */
 };
 
 /* Library version string, e.g. "pagedserve_b200 0.1.0 sm_100a". */
@@ -260,6 +268,38 @@ int psb_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, con
                       int32_t max_context, int32_t q_heads, int32_t layer, int32_t num_layers, int64_t num_blocks,
                       int32_t num_kv_heads, int32_t block_size, int32_t head_dim, int32_t dtype, float scale,
                       int32_t* error_flag, psb_stream_t stream);
+
+/*
+ * select_tokens: greedy next-token selection and the stop check of one decode
+ * step, for every row of the batch, in one launch.
+ *
+ * Replaces the reference's
+ *     tokens = logits[:, -1, :].argmax(dim=-1, keepdim=True)
+ * followed by its per-row host loop - token.item(), add_generated_token
+ * (which raises when no tokens remain), and the finish test
+ * ``token_id in eos_ids or request.remaining_tokens == 0``
+ * (pagedserve/engine/continuous_batcher.py:333-350, pagedserve/engine/request.py:84-106).
+ *
+ * logits     [batch, vocab] of ``dtype``, row stride ``row_stride`` elements
+ *            (>= vocab when batch > 1), unit element stride; for the
+ *            reference's [B, S, V] output pass the last position's rows
+ *            (base + (S-1)*V, row_stride = S*V).
+ * eos_ids    [num_eos] int64 (num_eos <= 64; may be NULL when 0)
+ * remaining  [batch] int32, in/out: tokens each request may still generate
+ *            (max_new_tokens - generated); decremented by one per row.
+ * tokens     [batch] int64, out: argmax index (first maximum; NaN counts as
+ *            the largest value, as torch.argmax does; -0.0 == +0.0)
+ * status     [batch] uint8, out: PSB_SELECT_* bits
+ * ctas_per_row  0 = chosen by the library, else 1..8 CTAs (one thread-block
+ *            cluster) per row.
+ * A row whose ``remaining`` is <= 0 on entry keeps it, gets
+ * PSB_SELECT_DONE | PSB_SELECT_LIMIT and raises PSB_DEVERR_LIMIT.
+ * Launched with programmatic dependent launch: a kernel that consumes
+ * ``tokens`` must wait (griddepcontrol.wait) before reading them.
+ */
+int psb_select_tokens(const void* logits, int64_t row_stride, int32_t batch, int32_t vocab, int32_t dtype,
+                      const int64_t* eos_ids, int32_t num_eos, int32_t* remaining, int64_t* tokens, uint8_t* status,
+                      int32_t ctas_per_row, int32_t* error_flag, psb_stream_t stream);
 
 /*
  * pack_step: GPU-side ragged-batch packer for one engine step.

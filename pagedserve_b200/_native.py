@@ -24,6 +24,7 @@ DEVERR_BITS = {
     8: "split-K work exceeded the workspace",
     16: "async wait exceeded its bound",
     32: "cu_seqlens malformed",
+    64: "a row had no tokens left to generate",
 }
 
 _c_void_p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -60,6 +61,9 @@ SIGNATURES = {
     "psb_varlen_prefill": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p,
         _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p, _c_void_p]),
+    "psb_select_tokens": (ctypes.c_int, [
+        _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,
+        _c_void_p]),
     "psb_pack_step": (ctypes.c_int, [
         _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p,
         _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p]),

@@ -20,7 +20,8 @@ std::mutex g_mu;
 std::unordered_map<int, int> g_sm_count;
 std::map<std::tuple<int, uintptr_t, size_t, int>, int> g_occ;  // (device, func, smem, threads) -> CTAs/SM
 std::set<std::pair<int, uintptr_t>> g_smem_raised;             // (device, func) with the smem ceiling raised
-std::set<std::pair<int, uintptr_t>> g_carveout_set;            // (device, func) preferring the full smem carve-out
+std::set<std::pair<int, uintptr_t>> g_carveout_set;      // (device, func) preferring the full smem carve-out
+std::set<std::pair<int, uintptr_t>> g_l1_set;            // (device, func) preferring the full L1 carve-out
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
@@ -67,6 +68,21 @@ bool prefer_max_shared(const void* func) {
       cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) {
     g_carveout_set.erase(key);
+    return record_cuda_error(e), false;
+  }
+  return true;
+}
+
+bool prefer_max_l1(const void* func) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const auto key = std::make_pair(dev, reinterpret_cast<uintptr_t>(func));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_l1_set.insert(key).second) return true;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxL1);
+  if (e != cudaSuccess) {
+    g_l1_set.erase(key);
     return record_cuda_error(e), false;
   }
   return true;

@@ -23,6 +23,13 @@ int device_sm_count();
 // them.
 bool prefer_max_shared(const void* func);
 
+// Ask for the largest L1 (smallest shared-memory) carve-out for ``func``
+// (once per device; overrides prefer_max_shared).  For kernels that stream
+// with plain global loads and use no shared memory: every load in flight
+// holds L1 space until its data returns, so L1 capacity bounds an SM's
+// bytes in flight.
+bool prefer_max_l1(const void* func);
+
 // CTAs of ``func`` that fit on one SM at ``threads`` threads and ``smem``
 // dynamic shared bytes under the full carve-out: registers (per warp, in
 // units of 256), shared memory (plus static and the per-CTA reservation),

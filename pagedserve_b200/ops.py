@@ -9,6 +9,9 @@
   prefill of pagedserve/attention/qwen_paged_attention.py:121-128)
 * ``pack_step``          GPU-side ragged-batch metadata for one engine step
   (replaces pagedserve/attention/triton_paged_decode.py:134-154)
+* ``select_tokens``      greedy next token + stop check of every row on the
+  device (replaces ``logits[:, -1, :].argmax`` and the per-row ``.item()``
+  loop of pagedserve/engine/continuous_batcher.py:333-350)
 
 Every function requires CUDA tensors, launches on the current stream and
 returns without synchronising.  There is no CPU path.
@@ -374,3 +377,58 @@ def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.T
         cu.data_ptr(), ctx.data_ptr(), slots.data_ptr(), pos.data_ptr(), tables.data_ptr(), out_width,
         _ptr(error_flag), _stream(dev)), "pack_step")
     return cu, ctx, slots, pos, tables
+
+
+SELECT_DONE, SELECT_EOS, SELECT_LIMIT = 1, 2, 4
+
+
+def select_tokens(logits: torch.Tensor, eos_ids: torch.Tensor, remaining: torch.Tensor,
+                  tokens: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                  error_flag: torch.Tensor | None = None, ctas_per_row: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Greedy next token of every row and the reference's stop test, in one launch.
+
+    ``logits`` is ``[B, V]`` or the model's ``[B, S, V]`` (the last position is
+    used, as ``logits[:, -1, :]``), unit stride along V.  ``eos_ids`` int64
+    ``[E]`` (E <= 64), ``remaining`` int32 ``[B]``: tokens each request may
+    still generate, decremented in place.  Returns ``(tokens [B] int64,
+    status [B] uint8)``: ``tokens`` is ``argmax(dim=-1)`` with torch's rules
+    (first maximum, NaN largest); ``status`` holds SELECT_DONE (the request
+    finishes: EOS or its last allowed token), SELECT_EOS, and SELECT_LIMIT
+    (no tokens were left: the reference's add_generated_token raises; the
+    row is also flagged in ``error_flag`` with 64).
+    """
+    _require_cuda(logits, eos_ids, remaining)
+    if logits.ndim == 3:
+        logits = logits[:, -1, :]
+    if logits.ndim != 2:
+        raise ValueError("logits must be [B, V] or [B, S, V]")
+    b, v = int(logits.shape[0]), int(logits.shape[1])
+    if v == 0:
+        raise ValueError("logits have an empty vocabulary axis")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    if eos_ids.dtype != torch.int64 or eos_ids.ndim != 1 or eos_ids.shape[0] > 64:
+        raise ValueError("eos_ids must be int64 [E] with E <= 64")
+    if not eos_ids.is_contiguous():
+        eos_ids = eos_ids.contiguous()
+    if remaining.dtype != torch.int32 or remaining.shape != (b,) or not remaining.is_contiguous():
+        raise ValueError("remaining must be a contiguous int32 [B] tensor (updated in place)")
+    if tokens is None:
+        tokens = torch.empty(b, dtype=torch.int64, device=logits.device)
+    if status is None:
+        status = torch.empty(b, dtype=torch.uint8, device=logits.device)
+    if tokens.dtype != torch.int64 or tokens.shape != (b,) or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous int64 [B] tensor")
+    if status.dtype != torch.uint8 or status.shape != (b,) or not status.is_contiguous():
+        raise ValueError("status must be a contiguous uint8 [B] tensor")
+    if not 0 <= ctas_per_row <= 8:
+        raise ValueError("ctas_per_row must be 0 (auto) or 1..8")
+    if b == 0:
+        return tokens, status
+    row_stride = int(logits.stride(0)) if b > 1 else v
+    lib = _native.load()
+    _native.check(lib.psb_select_tokens(
+        logits.data_ptr(), row_stride, b, v, dtype_code(logits.dtype), eos_ids.data_ptr() if eos_ids.numel() else None,
+        int(eos_ids.shape[0]), remaining.data_ptr(), tokens.data_ptr(), status.data_ptr(), ctas_per_row,
+        _ptr(error_flag), _stream(logits.device)), "select_tokens")
+    return tokens, status

@@ -71,6 +71,21 @@ def test_argument_checks_need_no_gpu():
                                   _native.PSB_BF16, 0.125, null, null) == _native.PSB_ERR_INVALID
     assert lib.psb_pack_step(null, 4, 1, null, null, null, 0, 0, 16, null, null, null, null, null, 4, null,
                              null) == _native.PSB_OK
+    # select_tokens: null buffers, too many EOS ids, a cluster wider than 8,
+    # overlapping rows and an empty vocabulary are rejected; an empty batch is a no-op
+    bf16 = _native.PSB_BF16
+    assert lib.psb_select_tokens(null, 8, 2, 8, bf16, null, 0, null, null, null, 0, null,
+                                 null) == _native.PSB_ERR_INVALID
+    assert lib.psb_select_tokens(null, 8, 0, 8, bf16, null, 0, null, null, null, 0, null, null) == _native.PSB_OK
+    assert lib.psb_select_tokens(null, 8, 0, 8, bf16, null, 65, null, null, null, 0, null,
+                                 null) == _native.PSB_ERR_INVALID
+    assert lib.psb_select_tokens(null, 8, 0, 8, bf16, null, 0, null, null, null, 9, null,
+                                 null) == _native.PSB_ERR_INVALID
+    assert lib.psb_select_tokens(null, 8, 0, 0, bf16, null, 0, null, null, null, 0, null,
+                                 null) == _native.PSB_ERR_INVALID
+    fake = 1 << 20  # never dereferenced: the stride check fails first
+    assert lib.psb_select_tokens(fake, 4, 2, 8, bf16, null, 0, fake, fake, fake, 0, null,
+                                 null) == _native.PSB_ERR_INVALID
 
 
 def test_ops_reject_cpu_tensors():
