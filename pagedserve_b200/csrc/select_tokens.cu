@@ -173,13 +173,17 @@ __device__ __forceinline__ float load_scalar(const __nv_bfloat16* p) {
   return lane_f<__nv_bfloat16>(__ldcs(reinterpret_cast<const unsigned short*>(p)), 0);
 }
 
-// Lane of vector r holding value key `k` first (r is known to hold it).
+// a equals the maximum m in the order of the keys: NaN matches NaN, and
+// -0.0 matches +0.0 (float equality already treats them alike)
+__device__ __forceinline__ bool same_value(float a, float m) { return m == m ? a == m : a != a; }
+
+// Lane of vector r holding the maximum m first (r is known to hold it).
 template <typename T>
-__device__ __forceinline__ int first_lane(const uint4& r, uint32_t k) {
+__device__ __forceinline__ int first_lane(const uint4& r, float m) {
   int j = 0;
 #pragma unroll
   for (int e = Vec<T>::N - 1; e >= 0; --e)
-    if (order_key(Vec<T>::at(r, e)) == k) j = e;
+    if (same_value(Vec<T>::at(r, e), m)) j = e;
   return j;
 }
 
@@ -277,18 +281,25 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
   const uint8_t* base = reinterpret_cast<const uint8_t*>(logits + lo);
   uint64_t policy = 0;
   if (lane == 0) policy = l2_policy_evict_first();
-  auto issue = [&](int j) {
-    const int ri = j / npc, t = j - ri * npc;
-    const int64_t row = cl + static_cast<int64_t>(ri) * ncl;
-    const int32_t v0 = w0 + t * kSlotVecs;
+  // lane 0's cursor: the next piece to copy (sequence number, row, piece of the row)
+  int pj = 0, pri = 0, pt = 0;
+  auto issue_next = [&]() {
+    const int64_t row = cl + static_cast<int64_t>(pri) * ncl;
+    const int32_t v0 = w0 + pt * kSlotVecs;
     const uint32_t bytes = static_cast<uint32_t>(min(kSlotVecs, w1 - v0)) * 16u;
-    uint64_t* bar = &full[warp][j % kSlots];
+    const int slot = pj % kSlots;
+    uint64_t* bar = &full[warp][slot];
     mbar_arrive_expect_tx(bar, bytes);
-    bulk_load(my_ring + (j % kSlots) * kSlotBytes, base + row * row_stride * static_cast<int64_t>(sizeof(T)) +
+    bulk_load(my_ring + slot * kSlotBytes, base + row * row_stride * static_cast<int64_t>(sizeof(T)) +
                   static_cast<int64_t>(v0) * 16, bytes, bar, policy);
+    ++pj;
+    if (++pt == npc) {
+      pt = 0;
+      ++pri;
+    }
   };
   if (lane == 0)
-    for (int j = 0; j < min(kSlots, total); ++j) issue(j);
+    for (int k = 0; k < min(kSlots, total); ++k) issue_next();
 
   // Lane state for the current row: its best value so far, the index of the
   // 16-byte vector holding it first (-1: the lane owns no vector of the
@@ -322,19 +333,18 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
     }
     // every lane has its vectors in registers: the slot may be refilled
     __syncwarp();
-    if (lane == 0 && j + kSlots < total) {
+    if (lane == 0 && pj < total) {  // pj == j + kSlots
       fence_proxy_async_smem();
-      issue(j + kSlots);
+      issue_next();
     }
     if (lane < nv) {  // the lane owns at least one vector of this piece
       const float pm = acc.result();
       // the row's first piece always sets the lane's record
       if (t == 0 || pm > bv || (pm != pm && bv == bv)) {
-        const uint32_t km = order_key(pm);
         int hit = 0;
 #pragma unroll
         for (int i = kVecPerLane - 1; i >= 0; --i)
-          if (lane + 32 * i < nv && order_key(Vec<T>::vmax(r[i])) == km) hit = i;
+          if (lane + 32 * i < nv && same_value(Vec<T>::vmax(r[i]), pm)) hit = i;
 #pragma unroll
         for (int i = 0; i < kVecPerLane; ++i)
           if (i == hit) bdata = r[i];
@@ -348,7 +358,7 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
       const uint32_t first_vec = __reduce_min_sync(
           0xFFFFFFFFu, (bvec >= 0 && lk == mk) ? static_cast<uint32_t>(bvec) : 0x7FFFFFFFu);
       if (bvec >= 0 && static_cast<uint32_t>(bvec) == first_vec)
-        wkeys[ri][warp] = pack_key(mk, lo + bvec * N + first_lane<T>(bdata, mk));
+        wkeys[ri][warp] = pack_key(mk, lo + bvec * N + first_lane<T>(bdata, bv));
       bv = -INFINITY;
       bvec = -1;
       t = 0;
@@ -448,7 +458,7 @@ __global__ void __launch_bounds__(kSelThreads) select_tokens_kernel(
           const float m = Vec<T>::vmax(r[u]);
           if (best.beaten_by(m)) {
             best.v = m;
-            best.i = i + first_lane<T>(r[u], order_key(m));
+            best.i = i + first_lane<T>(r[u], m);
           }
         }
       }
