@@ -278,7 +278,7 @@ int psb_paged_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, con
  * followed by its per-row host loop - token.item(), add_generated_token
  * (which raises when no tokens remain), and the finish test
  * ``token_id in eos_ids or request.remaining_tokens == 0``
- * (pagedserve/engine/continuous_batcher.py:333-350, pagedserve/engine/request.py:84-106).
+ * (pagedserve/engine/continuous_batcher.py:333-360, pagedserve/engine/request.py:84-106).
  *
  * logits     [batch, vocab] of ``dtype``, row stride ``row_stride`` elements
  *            (>= vocab when batch > 1), unit element stride; for the

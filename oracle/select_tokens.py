@@ -8,7 +8,7 @@ Restates in numpy what PagedServe does with a decode step's logits:
                         first index of the maximum, any NaN larger than every
                         number (the first NaN wins), -0.0 equal to +0.0.
 * ``select_tokens``  <- the per-row loop after it
-                        (pagedserve/engine/continuous_batcher.py:337-350):
+                        (pagedserve/engine/continuous_batcher.py:337-360):
                         ``request.add_generated_token(token_id)`` raises when
                         ``remaining_tokens <= 0`` (pagedserve/engine/request.py:99-106),
                         else the request finishes when

@@ -11,7 +11,7 @@ Public surface:
   tensor-level API over the C ABI (include/pagedserve_b200.h)
 * ``select_next_tokens`` / ``read_selection`` - the step's greedy argmax and
   stop test on the device, one host sync per batch (replaces the per-row
-  ``.item()`` loop of pagedserve/engine/continuous_batcher.py:333-350)
+  ``.item()`` loop of pagedserve/engine/continuous_batcher.py:333-360)
 * ``PagedKVCache`` and friends - host-side block bookkeeping with the
   reference's interface
 * ``SequenceDispatcher`` - places requests on the GPUs of a node (one

@@ -6,7 +6,7 @@
 // and then, per row on the host, reads the token with .item(), appends it to
 // the request (Request.add_generated_token raises when no tokens remain) and
 // finishes the request when the token is an EOS id or no tokens remain
-// (pagedserve/engine/continuous_batcher.py:333-350,
+// (pagedserve/engine/continuous_batcher.py:333-360,
 //  pagedserve/engine/request.py:84-106).  Here the argmax, the append's
 // limit check, the countdown and the stop test all run on the GPU; the host
 // reads B tokens and B status bytes with one copy instead of B syncs.

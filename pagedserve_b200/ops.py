@@ -11,7 +11,7 @@
   (replaces pagedserve/attention/triton_paged_decode.py:134-154)
 * ``select_tokens``      greedy next token + stop check of every row on the
   device (replaces ``logits[:, -1, :].argmax`` and the per-row ``.item()``
-  loop of pagedserve/engine/continuous_batcher.py:333-350)
+  loop of pagedserve/engine/continuous_batcher.py:333-360)
 
 Every function requires CUDA tensors, launches on the current stream and
 returns without synchronising.  There is no CPU path.

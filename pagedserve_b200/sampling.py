@@ -9,7 +9,7 @@ The reference ends every batched decode step with
         if token_id in eos_ids or request.remaining_tokens == 0:
             ...finish the request...
 
-(pagedserve/engine/continuous_batcher.py:333-350; the same loop in
+(pagedserve/engine/continuous_batcher.py:333-360; the same loop in
 pagedserve/model/engine.py:479-491).  ``select_next_tokens`` runs the argmax,
 the limit check, the countdown and the finish test for all rows in one
 kernel (psb_select_tokens); ``read_selection`` brings the tokens and the

@@ -11,7 +11,7 @@ zeros and all--inf rows) this evaluates the reference's own expression
 runs each row through the reference's ``Request`` class
 (pagedserve/engine/request.py): ``add_generated_token`` (which raises when no
 tokens remain) and the finish test ``token_id in eos_ids or
-request.remaining_tokens == 0`` (continuous_batcher.py:337-350).  Inputs and
+request.remaining_tokens == 0`` (continuous_batcher.py:337-360).  Inputs and
 outputs go to ``tests/golden/select_outputs.npz``; nothing on the GPU box
 reads the reference.
 """
