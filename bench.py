@@ -630,14 +630,20 @@ def run_b200(args, world, rank, local):
 
     from pagedserve_b200.attention import clear_metadata_cache
 
+    # the step's inputs land in device buffers the caller owns (copied from
+    # pinned host memory every step)
+    q_dev = torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16, device=device)
+    k_dev = torch.empty_like(w["new_k"])
+    v_dev = torch.empty_like(w["new_v"])
+
     def e2e_step(s):
         layer = s % LAYERS
         if layer == 0:  # a new decode iteration: block tables are rebuilt and copied once
             clear_metadata_cache(cache)
-        qd = q_host.to(device, non_blocking=True).unsqueeze(2)  # [B, Hq, 1, D]
-        kd = k_host.to(device, non_blocking=True)
-        vd = v_host.to(device, non_blocking=True)
-        o = paged_decode_attention_with_write(qd, kd, vd, cache, ids, positions, layer)
+        q_dev.copy_(q_host.view(batch, HQ, 1, D), non_blocking=True)
+        k_dev.copy_(k_host, non_blocking=True)
+        v_dev.copy_(v_host, non_blocking=True)
+        o = paged_decode_attention_with_write(q_dev, k_dev, v_dev, cache, ids, positions, layer)
         o_host.copy_(o, non_blocking=True)
 
     for s in range(min(args.warmup, 3)):

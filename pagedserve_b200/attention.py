@@ -39,22 +39,37 @@ _KEEP = 4  # metadata entries kept per cache (one per live batch shape)
 
 def _memo(cache, kind: str, request_ids, positions, device, build):
     """``build()``, or its result from an earlier call at the same cache
-    epoch for the same requests, positions and device."""
+    epoch for the same requests, positions and device.
+
+    The layer calls of one decode iteration pass the same lists: the last
+    result per kind is checked first with two list comparisons (C speed),
+    before the keyed store."""
     epoch = getattr(cache, "metadata_epoch", None)
     if epoch is None:
         return build()
+    dev = str(device)
+    lists = type(request_ids) is list and type(positions) is list
+    last = getattr(cache, "_psb_last", None)
+    if last is None:
+        last = cache._psb_last = {}
+    if lists:
+        hit = last.get(kind)
+        if hit is not None and hit[0] == epoch and hit[1] == dev and hit[2] == request_ids and hit[3] == positions:
+            return hit[4]
     store = getattr(cache, "_psb_metadata", None)
     if store is None:
         store = cache._psb_metadata = OrderedDict()
-    key = (kind, epoch, tuple(request_ids), tuple(int(p) for p in positions), str(device))
-    hit = store.get(key)
-    if hit is not None:
+    key = (kind, epoch, tuple(request_ids), tuple(int(p) for p in positions), dev)
+    value = store.get(key)
+    if value is not None:
         store.move_to_end(key)
-        return hit
-    value = build()
-    store[key] = value
-    while len(store) > _KEEP:
-        store.popitem(last=False)
+    else:
+        value = build()
+        store[key] = value
+        while len(store) > _KEEP:
+            store.popitem(last=False)
+    if lists:
+        last[kind] = (epoch, dev, list(request_ids), list(positions), value)
     return value
 
 
@@ -63,6 +78,9 @@ def clear_metadata_cache(cache) -> None:
     store = getattr(cache, "_psb_metadata", None)
     if store is not None:
         store.clear()
+    last = getattr(cache, "_psb_last", None)
+    if last is not None:
+        last.clear()
 
 
 def _host_metadata(cache, request_ids, positions, device):
@@ -75,19 +93,34 @@ def _host_metadata(cache, request_ids, positions, device):
 
 
 def _build_metadata(cache, request_ids, positions, device):
-    lengths = np.empty(len(request_ids), dtype=np.int32)
-    tables = []
-    for row, (rid, pos) in enumerate(zip(request_ids, positions)):
-        count = cache.token_count(rid)
-        if not 0 <= pos < count:
-            raise ValueError(f"Invalid position {pos} for {rid}")
-        lengths[row] = pos + 1
-        tables.append(cache.get_block_table(rid).get_blocks())
-    width = max(len(t) for t in tables)
-    packed = np.zeros((len(tables), width + 1), dtype=np.int32)  # [table | length]
-    for row, t in enumerate(tables):
-        packed[row, : len(t)] = t
-    packed[:, width] = lengths
+    if hasattr(cache, "token_counts") and hasattr(cache, "table_rows"):
+        # this package's PagedKVCache: vectorised over its table store
+        counts = cache.token_counts(request_ids)
+        pos = np.asarray(positions, dtype=np.int64)
+        bad = np.flatnonzero((pos < 0) | (pos >= counts))
+        if bad.size:
+            row = int(bad[0])
+            raise ValueError(f"Invalid position {positions[row]} for {request_ids[row]}")
+        table = cache.table_rows(request_ids)
+        width = table.shape[1]
+        packed = np.empty((len(request_ids), width + 1), dtype=np.int32)  # [table | length]
+        packed[:, :width] = table
+        packed[:, width] = pos + 1
+    else:
+        # any cache with the reference's interface
+        lengths = np.empty(len(request_ids), dtype=np.int32)
+        tables = []
+        for row, (rid, pos) in enumerate(zip(request_ids, positions)):
+            count = cache.token_count(rid)
+            if not 0 <= pos < count:
+                raise ValueError(f"Invalid position {pos} for {rid}")
+            lengths[row] = pos + 1
+            tables.append(cache.get_block_table(rid).get_blocks())
+        width = max(len(t) for t in tables)
+        packed = np.zeros((len(tables), width + 1), dtype=np.int32)  # [table | length]
+        for row, t in enumerate(tables):
+            packed[row, : len(t)] = t
+        packed[:, width] = lengths
     host = torch.from_numpy(packed)
     if device.type == "cuda":
         host = host.pin_memory()

@@ -19,6 +19,7 @@ returns without synchronising.  There is no CPU path.
 
 from __future__ import annotations
 
+import functools
 import math
 import threading
 
@@ -181,6 +182,7 @@ class DecodeWorkspace:
         return self.buffer
 
 
+@functools.lru_cache(maxsize=256)
 def decode_workspace_bytes(batch: int, q_heads: int, hkv: int, head_dim: int, block_size: int, max_context: int,
                            dtype: torch.dtype) -> int:
     lib = _native.load()

@@ -99,7 +99,8 @@ class BlockTable:
 
     def __init__(self) -> None:
         self._blocks: list[int] = []
-        self._owner: "PagedKVCache | None" = None  # told of every change (metadata epoch)
+        self._owner: "PagedKVCache | None" = None  # told of every change (metadata epoch, table store)
+        self._row = -1                              # this table's row in the owner's table store
 
     @property
     def num_blocks(self) -> int:
@@ -110,6 +111,7 @@ class BlockTable:
             raise ValueError("physical_block_id cannot be negative")
         self._blocks.append(physical_block_id)
         if self._owner is not None:
+            self._owner._store_put(self._row, len(self._blocks) - 1, physical_block_id)
             self._owner._epoch += 1
 
     def get_physical_block(self, logical_block_id: int) -> int:
@@ -123,6 +125,7 @@ class BlockTable:
     def clear(self) -> None:
         self._blocks.clear()
         if self._owner is not None:
+            self._owner._store_clear(self._row)
             self._owner._epoch += 1
 
 
@@ -196,6 +199,14 @@ class PagedKVCache:
         self._tables: dict[str, BlockTable] = {}
         self._counts: dict[str, int] = {}
         self._epoch = 0
+        # Table store: one zero-padded int32 row of block ids per live
+        # request, kept in step with the BlockTables, so a batch's block table
+        # is one gather instead of a list-to-array copy per request.
+        self._store = np.zeros((16, 16), dtype=np.int32)
+        self._store_blocks = np.zeros(16, dtype=np.int64)   # blocks per store row
+        self._store_tokens = np.zeros(16, dtype=np.int64)   # token count per store row
+        self._free_rows: list[int] = []
+        self._rows_used = 0
 
     # -- allocation ---------------------------------------------------------
     def allocate(self, request_id: str, num_tokens: int) -> None:
@@ -203,12 +214,15 @@ class PagedKVCache:
             raise ValueError(f"Request {request_id!r} already exists")
         if num_tokens < 0:
             raise ValueError("num_tokens cannot be negative")
+        blocks = self.block_manager.allocate(request_id=request_id, num_tokens=num_tokens)
         table = BlockTable()
-        for blk in self.block_manager.allocate(request_id=request_id, num_tokens=num_tokens):
-            table.append(blk)
         table._owner = self
+        table._row = self._store_row()
+        for blk in blocks:
+            table.append(blk)
         self._tables[request_id] = table
         self._counts[request_id] = num_tokens
+        self._store_tokens[table._row] = num_tokens
         self._epoch += 1
 
     def append_tokens(self, request_id: str, num_tokens: int) -> None:
@@ -224,14 +238,55 @@ class PagedKVCache:
             for blk in self.block_manager.allocate_blocks(request_id=request_id, num_blocks=extra):
                 self._tables[request_id].append(blk)
         self._counts[request_id] = old + num_tokens
+        self._store_tokens[self._tables[request_id]._row] = old + num_tokens
         self._epoch += 1
 
     def free(self, request_id: str) -> None:
         self._validate_request(request_id)
-        self._tables.pop(request_id)._owner = None
+        table = self._tables.pop(request_id)
+        self._store_clear(table._row)
+        self._free_rows.append(table._row)
+        table._owner, table._row = None, -1
         del self._counts[request_id]
         self.block_manager.free(request_id)
         self._epoch += 1
+
+    # -- table store -------------------------------------------------------------
+    def _store_row(self) -> int:
+        if self._free_rows:
+            return self._free_rows.pop()
+        row = self._rows_used
+        self._rows_used += 1
+        if row >= self._store.shape[0]:
+            grow = self._store.shape[0]
+            self._store = np.concatenate([self._store, np.zeros_like(self._store[:grow])])
+            self._store_blocks = np.concatenate([self._store_blocks, np.zeros(grow, dtype=np.int64)])
+            self._store_tokens = np.concatenate([self._store_tokens, np.zeros(grow, dtype=np.int64)])
+        return row
+
+    def _store_put(self, row: int, index: int, block: int) -> None:
+        if index >= self._store.shape[1]:
+            width = max(2 * self._store.shape[1], index + 1)
+            wider = np.zeros((self._store.shape[0], width), dtype=np.int32)
+            wider[:, : self._store.shape[1]] = self._store
+            self._store = wider
+        self._store[row, index] = block
+        self._store_blocks[row] = index + 1
+
+    def _store_clear(self, row: int) -> None:
+        self._store[row, :] = 0
+        self._store_blocks[row] = 0
+        self._store_tokens[row] = 0
+
+    def _rows_of(self, request_ids) -> np.ndarray:
+        rows = np.empty(len(request_ids), dtype=np.int64)
+        tables = self._tables
+        for i, r in enumerate(request_ids):
+            t = tables.get(r)
+            if t is None:
+                raise KeyError(f"Unknown request: {r!r}")
+            rows[i] = t._row
+        return rows
 
     # -- queries ---------------------------------------------------------------
     def get_block_table(self, request_id: str) -> BlockTable:
@@ -304,10 +359,19 @@ class PagedKVCache:
         return block * self.block_size + offset
 
     def table_rows(self, request_ids, width: int | None = None) -> np.ndarray:
-        """Zero-padded int32 ``[B, width]`` block table of ``request_ids``."""
-        tables = [self.get_block_table(r)._blocks for r in request_ids]
-        width = max((len(t) for t in tables), default=0) if width is None else width
-        out = np.zeros((len(tables), max(width, 1)), dtype=np.int32)
-        for i, t in enumerate(tables):
-            out[i, : len(t)] = t
+        """Zero-padded int32 ``[B, width]`` block table of ``request_ids``
+        (width: the longest of their tables by default)."""
+        rows = self._rows_of(request_ids)
+        if width is None:
+            width = int(self._store_blocks[rows].max()) if len(rows) else 0
+        width = max(width, 1)
+        have = min(width, self._store.shape[1])
+        if have == width:
+            return self._store[rows, :width]
+        out = np.zeros((len(rows), width), dtype=np.int32)
+        out[:, :have] = self._store[rows, :have]
         return out
+
+    def token_counts(self, request_ids) -> np.ndarray:
+        """int64 ``[B]`` token counts of ``request_ids``."""
+        return self._store_tokens[self._rows_of(request_ids)]

@@ -270,3 +270,70 @@ def test_host_metadata_without_epoch_rebuilds():
     b = attention._host_metadata(plain, ["r"], [5], torch.device("cpu"))
     assert a[0] is not b[0] and torch.equal(a[0], b[0])
     assert not hasattr(plain, "_psb_metadata")
+
+
+def test_table_store_follows_every_change():
+    """table_rows / token_counts (the vectorised store) equal the per-request
+    BlockTables through allocation, growth past the store's width, frees,
+    row reuse and direct table edits."""
+    rng = np.random.default_rng(7)
+    c = PagedKVCache(num_blocks=4096, num_layers=1, num_kv_heads=1, head_dim=8, block_size=4, dtype=torch.float32,
+                     device="cpu", free_order=rng.permutation(4096))
+    live: dict[str, int] = {}
+    for step in range(400):
+        op = rng.integers(0, 3)
+        if op == 0 or not live:
+            rid = f"r{step}"
+            n = int(rng.integers(0, 70))
+            c.allocate(rid, n)
+            live[rid] = n
+        elif op == 1:
+            rid = list(live)[int(rng.integers(0, len(live)))]
+            k = int(rng.integers(0, 90))
+            c.append_tokens(rid, k)
+            live[rid] += k
+        else:
+            rid = list(live)[int(rng.integers(0, len(live)))]
+            c.free(rid)
+            del live[rid]
+        if live and step % 7 == 0:
+            ids = list(live)
+            rng.shuffle(ids)
+            rows = c.table_rows(ids)
+            width = max(1, max(c.get_block_table(r).num_blocks for r in ids))
+            want = np.zeros((len(ids), width), dtype=np.int32)
+            for i, r in enumerate(ids):
+                b = c.get_block_table(r).get_blocks()
+                want[i, : len(b)] = b
+            assert np.array_equal(rows, want)
+            assert c.token_counts(ids).tolist() == [live[r] for r in ids]
+            assert np.array_equal(c.table_rows(ids, width=width + 3)[:, :width], want)
+            assert not c.table_rows(ids, width=width + 3)[:, width:].any()
+    rid = next(iter(live))
+    c.get_block_table(rid).append(4000)                # a caller's direct edit reaches the store
+    assert c.table_rows([rid])[0, c.get_block_table(rid).num_blocks - 1] == 4000
+    with pytest.raises(KeyError, match="Unknown request"):
+        c.table_rows([rid, "nope"])
+
+
+def test_host_metadata_fast_path_sees_list_changes():
+    """The last-call shortcut compares list contents, so an id list or a
+    position list changed in place between calls is never served stale."""
+    from pagedserve_b200 import attention
+    c = PagedKVCache(num_blocks=32, num_layers=1, num_kv_heads=1, head_dim=8, block_size=4, dtype=torch.float32,
+                     device="cpu")
+    for rid, n in (("x", 5), ("y", 9), ("z", 2)):
+        c.allocate(rid, n)
+    dev = torch.device("cpu")
+    ids, pos = ["x", "y"], [4, 8]
+    t1, l1, _ = attention._host_metadata(c, ids, pos, dev)
+    assert attention._host_metadata(c, ids, pos, dev)[0] is t1          # same lists: reused
+    pos[0] = 2
+    _, l2, _ = attention._host_metadata(c, ids, pos, dev)
+    assert l2.tolist() == [3, 9]
+    ids[1] = "z"
+    pos[1] = 1
+    t3, l3, _ = attention._host_metadata(c, ids, pos, dev)
+    assert l3.tolist() == [3, 2] and t3.tolist()[1][: 1] == c.get_block_table("z").get_blocks()
+    with pytest.raises(ValueError, match="Invalid position 7 for z"):
+        attention._host_metadata(c, ["x", "z"], [0, 7], dev)
