@@ -622,48 +622,77 @@ def run_b200(args, world, rank, local):
         raise RuntimeError(f"device error flag {int(err.item())}")
 
     # ---- end to end through the reference-facing API, host buffers -------
+    # Every step copies its inputs (q, new k, new v: one pinned staging
+    # buffer) to the device and its output back to pinned host memory.  The
+    # uploads run on their own stream into two alternating device buffers
+    # and the downloads on a third, so step s + 1's upload and step s - 1's
+    # download overlap step s's kernel, as a serving loop pipelines them.
     cache, ids, positions = w["cache"], w["ids"], w["positions"]
-    q_host = w["q"].cpu().pin_memory()
-    k_host = w["new_k"].cpu().pin_memory()
-    v_host = w["new_v"].cpu().pin_memory()
-    o_host = torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory()
+    q_bytes, kv_bytes = w["q"].numel() * 2, w["new_k"].numel() * 2
+    in_host = torch.empty(q_bytes + 2 * kv_bytes, dtype=torch.uint8).pin_memory()
+    in_host[:q_bytes].view(torch.bfloat16).copy_(w["q"].reshape(-1).cpu())
+    in_host[q_bytes:q_bytes + kv_bytes].view(torch.bfloat16).copy_(w["new_k"].reshape(-1).cpu())
+    in_host[q_bytes + kv_bytes:].view(torch.bfloat16).copy_(w["new_v"].reshape(-1).cpu())
+    in_dev = [torch.empty_like(in_host, device=device) for _ in range(2)]
+    views = [(buf[:q_bytes].view(torch.bfloat16).view(batch, HQ, 1, D),
+              buf[q_bytes:q_bytes + kv_bytes].view(torch.bfloat16).view(batch, HKV, D),
+              buf[q_bytes + kv_bytes:].view(torch.bfloat16).view(batch, HKV, D)) for buf in in_dev]
+    o_host = [torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    compute = torch.cuda.current_stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    o_keep = [None, None]
 
     from pagedserve_b200.attention import clear_metadata_cache
 
-    # the step's inputs land in device buffers the caller owns (copied from
-    # pinned host memory every step)
-    q_dev = torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16, device=device)
-    k_dev = torch.empty_like(w["new_k"])
-    v_dev = torch.empty_like(w["new_v"])
-
     def e2e_step(s):
-        layer = s % LAYERS
+        i, layer = s % 2, s % LAYERS
         if layer == 0:  # a new decode iteration: block tables are rebuilt and copied once
             clear_metadata_cache(cache)
-        q_dev.copy_(q_host.view(batch, HQ, 1, D), non_blocking=True)
-        k_dev.copy_(k_host, non_blocking=True)
-        v_dev.copy_(v_host, non_blocking=True)
-        o = paged_decode_attention_with_write(q_dev, k_dev, v_dev, cache, ids, positions, layer)
-        o_host.copy_(o, non_blocking=True)
+        torch.cuda.set_stream(s_up)
+        if s >= 2:
+            s_up.wait_event(ev_done[i])  # step s - 2's kernel has read this input buffer
+        in_dev[i].copy_(in_host, non_blocking=True)
+        ev_in[i].record(s_up)
+        torch.cuda.set_stream(compute)
+        compute.wait_event(ev_in[i])
+        if s >= 2:
+            # step s - 2's output has been read back: only now may its memory
+            # go to this step's output
+            compute.wait_event(ev_out[i])
+        o_keep[i] = None
+        qd, kd, vd = views[i]
+        o = paged_decode_attention_with_write(qd, kd, vd, cache, ids, positions, layer)
+        o_keep[i] = o
+        ev_done[i].record(compute)
+        torch.cuda.set_stream(s_down)
+        s_down.wait_event(ev_done[i])
+        o_host[i].copy_(o, non_blocking=True)
+        ev_out[i].record(s_down)
+        torch.cuda.set_stream(compute)
 
-    for s in range(min(args.warmup, 3)):
+    for s in range(min(args.warmup, 3) * 2):
         e2e_step(s)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
-    e_start.record()
+    e_start.record(compute)
+    s_up.wait_stream(compute)
     for s in range(args.steps):
         e2e_step(s)
-    e_end.record()
+    compute.wait_stream(s_down)
+    e_end.record(compute)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     width = cache.table_rows(ids).shape[1]
     iterations = -(-args.steps // LAYERS)  # metadata copies inside the timed region
     meta_bytes = 4 * batch * (width + 1)  # table + lengths
-    h2d = (q_host.numel() + k_host.numel() + v_host.numel()) * 2 + meta_bytes * iterations / args.steps
-    d2h = o_host.numel() * 2
+    h2d = in_host.numel() + meta_bytes * iterations / args.steps
+    d2h = o_host[0].numel() * 2
 
     # ---- packed prefill (one engine iteration's attention and KV write) ------
     prefill = run_prefill(args, device, 2000 + rank)
@@ -725,10 +754,11 @@ def run_b200(args, world, rank, local):
                          "decode_only_note": "decode + combine without the new-token store, same graphs"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
-                    "path": "per layer call: q, new k, new v copied from pinned host buffers, "
+                    "path": "per layer call: q, new k, new v copied from one pinned host staging buffer, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
-                            f"one launch), output copied back; block tables built and copied once per {LAYERS}-layer "
-                            "iteration"},
+                            "one launch), output copied back to pinned host memory; uploads and downloads on their "
+                            "own streams (two alternating device input buffers), so they overlap the neighbouring "
+                            f"steps' kernels; block tables built and copied once per {LAYERS}-layer iteration"},
             "gpu_launches": 2 * args.steps,
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
             "clocks": clocks.summary(),

@@ -136,8 +136,7 @@ def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str
     """
     tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
     kv = cache.kv_cache
-    return ops.paged_decode(query, kv.k_cache, kv.v_cache, tables, lengths, layer,
-                            max_context=width * cache.block_size)
+    return ops._decode_checked(query, kv.k_cache, kv.v_cache, tables, lengths, layer, width * cache.block_size)
 
 
 def _validated_metadata(query, cache, request_ids, positions, layer):
@@ -198,8 +197,8 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     if key.shape[0] != query.shape[0] or value.shape[0] != query.shape[0]:
         raise ValueError("Request IDs and positions must match batch size")
     tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
-    return ops.paged_decode(query, kv.k_cache, kv.v_cache, tables, lengths, layer,
-                            max_context=width * cache.block_size, new_key=key, new_value=value)
+    return ops._decode_checked(query, kv.k_cache, kv.v_cache, tables, lengths, layer, width * cache.block_size,
+                               new_key=key, new_value=value)
 
 
 def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], layer: int, key: torch.Tensor,

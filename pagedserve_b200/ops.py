@@ -37,7 +37,15 @@ def dtype_code(dtype: torch.dtype) -> int:
         raise ValueError(f"Unsupported dtype {dtype}") from None
 
 
+try:  # the raw handle of the current stream, without building a Stream object (as torch's own codegen does)
+    from torch._C import _cuda_getCurrentRawStream as _raw_stream
+except ImportError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def _stream(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -261,6 +269,52 @@ def paged_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         v_cache.data_ptr(), block_tables.data_ptr(), block_tables.stride(0), context_lens.data_ptr(), bsz, hq, layer,
         nl, nb, hkv, bs, d, dtype_code(q3.dtype), int(max_context), scale, workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), _ptr(error_flag), _stream(query.device)), "paged_decode")
+    return out
+
+
+def _decode_checked(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, tables: torch.Tensor,
+                    lengths: torch.Tensor, layer: int, max_context: int, new_key: torch.Tensor | None = None,
+                    new_value: torch.Tensor | None = None) -> torch.Tensor:
+    """paged_decode for the reference-facing wrappers, whose arguments are
+    already checked: ``query [B, Hq, 1, D]`` on the pools' device with their
+    dtype, contiguous pools, device tables ``[B, M]`` int32 with unit inner
+    stride and contiguous int32 lengths from the metadata builder, and new
+    rows of shape ``[B, Hkv(, 1), D]`` and the pools' dtype.  Only what the
+    launch itself needs is looked at (the public ``paged_decode`` repeats
+    every check; this path runs once per layer per decode iteration)."""
+    nl, nb, hkv, bs, d = k_cache.shape
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("KV pools must be contiguous")
+    if query.stride(3) != 1:
+        query = query.contiguous()
+    bsz, hq = query.shape[0], query.shape[1]
+    out = torch.empty_like(query)
+    need = decode_workspace_bytes(bsz, hq, hkv, d, bs, max_context, query.dtype)
+    ws = DecodeWorkspace.for_device(query.device).get(need, bsz, hkv)
+    lib = _native.load()
+    dt = _DTYPES[query.dtype]
+    stream = _stream(query.device)
+    scale = 1.0 / math.sqrt(d)
+    if new_key is None:
+        _native.check(lib.psb_paged_decode(
+            query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+            k_cache.data_ptr(), v_cache.data_ptr(), tables.data_ptr(), tables.stride(0), lengths.data_ptr(), bsz, hq,
+            layer, nl, nb, hkv, bs, d, dt, max_context, scale, ws.data_ptr(), ws.numel(), None, stream),
+            "paged_decode")
+        return out
+    if new_key.device != query.device or new_value.device != query.device:
+        raise ValueError("new K/V must be on the query's device")
+    nk = new_key.squeeze(2) if new_key.ndim == 4 else new_key
+    nv = new_value.squeeze(2) if new_value.ndim == 4 else new_value
+    if nk.stride(2) != 1:
+        nk = nk.contiguous()
+    if nv.stride(2) != 1:
+        nv = nv.contiguous()
+    _native.check(lib.psb_paged_decode_append(
+        query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(), nk.data_ptr(), nk.stride(0), nk.stride(1), nv.data_ptr(), nv.stride(0),
+        nv.stride(1), tables.data_ptr(), tables.stride(0), lengths.data_ptr(), bsz, hq, layer, nl, nb, hkv, bs, d, dt,
+        max_context, scale, ws.data_ptr(), ws.numel(), None, stream), "paged_decode_append")
     return out
 
 
