@@ -86,6 +86,36 @@ constexpr uint32_t kPoolTile = kPoolBlock * kDim * 2;  // bytes of one (block, k
 // PAGED (psb_paged_prefill): K/V come from the pools through the block table,
 // four pool tiles per 64-key step, and a sequence's query rows are the last
 // positions of its context; otherwise from the packed k/v rows of the batch.
+
+// Packed fp32 pairs (sm_100 f32x2 instructions): the exponent arguments and
+// the row sum take one instruction per two scores, and the row max one
+// three-input max per two scores (2 % off the 16K-token pack).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T, bool PAGED>
 __global__ void __launch_bounds__(kTcThreads, 2)
     prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
@@ -458,17 +488,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         // keys past this row's position or past the context only occur in the last steps
         const int lim = min(ti.start + qrow, ti.ctx - 1) - j * kBN;  // last valid key column
-        float mx = -INFINITY;
-        if (lim >= kBN - 1) {
+        if (lim < kBN - 1) {
 #pragma unroll
-          for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c) {
+          for (int c = 0; c < kBN; ++c)
             if (c > lim) sr[c] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(sr[c]));
-          }
         }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kBN; c += 4) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        }
+        const float mx = fmaxf(mx0, mx1);
         // lazy max: move it (and rescale O and the sum) only when the row max
         // grew by more than 2^kRescaleLog2; the warp's TMEM access is collective
         const float mxs = mx * sc;
@@ -496,15 +527,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           ms = ms_new;
         }
         const float mu = ms == -INFINITY ? 0.f : ms;  // rows with nothing valid yet stay zero
-        float rs = 0.f;
         uint32_t pk[kBN / 2];
+        const uint64_t sc2 = pk2(sc, sc), nmu2 = pk2(-mu, -mu);
+        uint64_t rs2 = pk2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < kBN; c += 2) {
-          const float x0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sc, -mu));
-          const float x1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sc, -mu));
-          rs += x0 + x1;
+          const float2 a = up2(ffma2(pk2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sc2, nmu2));
+          const float x0 = ex2_approx(a.x);
+          const float x1 = ex2_approx(a.y);
+          rs2 = fadd2(rs2, pk2(x0, x1));
           pk[c / 2] = pack2<T>(x0, x1);
         }
+        const float2 rsp = up2(rs2);
+        const float rs = rsp.x + rsp.y;
         l_run += rs;
         // P buffer g & 1 held P of step g - 2: wait for that P.V (normally long
         // done; P.V of step g cannot start before this thread's arrival below,
