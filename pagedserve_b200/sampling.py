@@ -19,6 +19,7 @@ raises the reference's error when a row had no tokens left.
 
 from __future__ import annotations
 
+import threading
 from typing import Iterable, Sequence
 
 import torch
@@ -62,14 +63,32 @@ def select_next_tokens(logits: torch.Tensor, eos_ids: torch.Tensor, remaining: t
     return tokens.view(-1, 1), status
 
 
+_pinned = threading.local()
+
+
+def _staging(n: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Pinned host buffers for ``n`` tokens and ``n`` status bytes, kept per
+    thread and grown on demand: pinning host memory costs far more than the
+    copy, and read_selection's copies have completed before it returns, so
+    the next call on the same thread may reuse them."""
+    bufs = getattr(_pinned, "bufs", None)
+    if bufs is None or bufs[0].numel() < n:
+        size = max(n, 256)
+        bufs = (torch.empty(size, dtype=torch.int64, pin_memory=True),
+                torch.empty(size, dtype=torch.uint8, pin_memory=True))
+        _pinned.bufs = bufs
+    return bufs[0][:n], bufs[1][:n]
+
+
 def read_selection(tokens: torch.Tensor, status: torch.Tensor) -> tuple[list[int], list[bool]]:
     """Host copy of one step's selection: (token ids, finished flags).
 
     One synchronisation for the batch.  Raises ``RuntimeError`` with the
     reference's message (request.py:105-106) when a row had no tokens left.
     """
-    host_t = torch.empty(tokens.numel(), dtype=torch.int64, pin_memory=True)
-    host_s = torch.empty(status.numel(), dtype=torch.uint8, pin_memory=True)
+    if tokens.numel() != status.numel():
+        raise ValueError("tokens and status differ in length")
+    host_t, host_s = _staging(tokens.numel())
     host_t.copy_(tokens.reshape(-1), non_blocking=True)
     host_s.copy_(status.reshape(-1), non_blocking=True)
     torch.cuda.current_stream(tokens.device).synchronize()
