@@ -26,11 +26,13 @@
 // contiguous part of that slice, which it streams through two 4 KB
 // shared-memory slots with bulk async copies it issues itself (no cross-warp
 // synchronisation).  Per piece: a branch-free packed maximum (max.NaN on
-// bf16x2 / f16x2 / f32) of each lane's vectors, and only when it beats the
-// lane's record, a lane-local rescan of those vectors (still in registers).
-// The lanes' records are merged once per row, the warps' results in their
-// CTA, each CTA stores its per-row result into CTA 0's shared memory, and
-// CTA 0 finishes the rows after the cluster barrier.
+// bf16x2 / f16x2 / f32) of each lane's vectors; the lane keeps its record
+// value and the piece where it first reached it.  At the end of a row the
+// warp takes the maximum over its lanes and the earliest piece where a lane
+// reached it, and only those lanes read their vectors of that piece again
+// (from global memory: 128 bytes each) to find the first index.  The warps'
+// results meet in their CTA, each CTA stores its per-row result into CTA 0's
+// shared memory, and CTA 0 finishes the rows after the cluster barrier.
 //
 // Register kernel (rows off a 16-byte boundary): grid (C, B), one cluster
 // per row; each thread keeps a running (value, first index) over its
@@ -54,10 +56,15 @@ namespace {
 constexpr int kSelThreads = 256;
 constexpr int kSelUnroll = 4;
 constexpr int kMaxCluster = 8;
-// CTAs per row when the caller leaves it to the library: on the 151936-entry
-// bf16 vocabulary, 6 measured fastest or within 1 % of it at 128 and 256 rows
-// (128: 12.95 us vs 13.7 - 16.1 for 1, 2, 4, 8; 256: 21.5 us vs 21.3 - 27.4).
-constexpr int kAutoCluster = 6;
+// CTAs per row when the caller leaves it to the library.  On the
+// 151936-entry bf16 vocabulary, 2 measured within 0.5 % of the fastest at 128
+// and 256 rows (128: 12.43 us, 1: 12.40, 6: 12.65, 4: 14.0, 8: 14.8; 256:
+// 18.98 us, 1: 18.91, 6: 19.76, 4: 19.93, 8: 24.7): fewer, longer row
+// slices per warp amortise the per-row merge.  Small batches spread each row
+// wider so the grid still covers the GPU.
+constexpr int kAutoCluster = 2;
+constexpr int kAutoClusterSmall = 6;
+constexpr int kSmallBatch = 64;
 constexpr int kMaxEos = 64;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kSlotBytes = 4096;                  // one piece of a warp's stream
@@ -301,13 +308,12 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
   if (lane == 0)
     for (int k = 0; k < min(kSlots, total); ++k) issue_next();
 
-  // Lane state for the current row: its best value so far, the index of the
-  // 16-byte vector holding it first (-1: the lane owns no vector of the
-  // row), and that vector.  A lane's vectors arrive in increasing index
-  // order, so only a strictly larger value (or a first NaN) replaces it.
+  // Lane state for the current row: its best value so far and the piece
+  // where it first reached it (-1: the lane owns no vector of the row).  A
+  // lane's pieces arrive in increasing index order, so only a strictly larger
+  // value (or a first NaN) replaces the record.
   float bv = -INFINITY;
-  int32_t bvec = -1;
-  uint4 bdata = make_uint4(0u, 0u, 0u, 0u);
+  int bpiece = -1;
   int ri = 0, t = 0;  // row and piece of piece j
   for (int j = 0; j < total; ++j) {
     const int slot = j % kSlots;
@@ -339,28 +345,38 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
     }
     if (lane < nv) {  // the lane owns at least one vector of this piece
       const float pm = acc.result();
-      // the row's first piece always sets the lane's record
-      if (t == 0 || pm > bv || (pm != pm && bv == bv)) {
-        int hit = 0;
-#pragma unroll
-        for (int i = kVecPerLane - 1; i >= 0; --i)
-          if (lane + 32 * i < nv && same_value(Vec<T>::vmax(r[i]), pm)) hit = i;
-#pragma unroll
-        for (int i = 0; i < kVecPerLane; ++i)
-          if (i == hit) bdata = r[i];
+      if (bpiece < 0 || pm > bv || (pm != pm && bv == bv)) {
         bv = pm;
-        bvec = v0 + lane + 32 * hit;
+        bpiece = t;
       }
     }
     if (++t == npc) {  // this warp's last piece of the row: merge the lanes
-      const uint32_t lk = bvec >= 0 ? order_key(bv) : 0u;
+      const uint32_t lk = bpiece >= 0 ? order_key(bv) : 0u;
       const uint32_t mk = __reduce_max_sync(0xFFFFFFFFu, lk);
-      const uint32_t first_vec = __reduce_min_sync(
-          0xFFFFFFFFu, (bvec >= 0 && lk == mk) ? static_cast<uint32_t>(bvec) : 0x7FFFFFFFu);
-      if (bvec >= 0 && static_cast<uint32_t>(bvec) == first_vec)
-        wkeys[ri][warp] = pack_key(mk, lo + bvec * N + first_lane<T>(bdata, bv));
+      // the earliest piece in which a lane reached the row's maximum; a lane
+      // that reached it only later holds smaller values in every earlier piece
+      const uint32_t pmin =
+          __reduce_min_sync(0xFFFFFFFFu, (bpiece >= 0 && lk == mk) ? static_cast<uint32_t>(bpiece) : 0x7FFFFFFFu);
+      uint32_t f = 0x7FFFFFFFu;
+      if (bpiece >= 0 && lk == mk && static_cast<uint32_t>(bpiece) == pmin) {
+        // this lane's vectors of that piece, read again (a few lanes per row)
+        const int32_t pv0 = w0 + static_cast<int32_t>(pmin) * kSlotVecs;
+        const int pnv = min(kSlotVecs, w1 - pv0);
+        const uint4* src = reinterpret_cast<const uint4*>(logits + (cl + static_cast<int64_t>(ri) * ncl) * row_stride +
+                                                          lo) + pv0;
+#pragma unroll
+        for (int i = 0; i < kVecPerLane; ++i) {
+          const int v = lane + 32 * i;
+          if (f == 0x7FFFFFFFu && v < pnv) {
+            const uint4 x = __ldg(src + v);
+            if (same_value(Vec<T>::vmax(x), bv)) f = static_cast<uint32_t>(lo + (pv0 + v) * N + first_lane<T>(x, bv));
+          }
+        }
+      }
+      f = __reduce_min_sync(0xFFFFFFFFu, f);
+      if (lane == 0) wkeys[ri][warp] = pack_key(mk, static_cast<int32_t>(f));
       bv = -INFINITY;
-      bvec = -1;
+      bpiece = -1;
       t = 0;
       ++ri;
     }
@@ -569,7 +585,7 @@ int launch_select(const void* logits, int64_t row_stride, int32_t batch, int32_t
                   bool aligned, const int64_t* eos, int32_t num_eos, int32_t* remaining, int64_t* tokens,
                   uint8_t* status, int32_t* err, cudaStream_t s) {
   const int esz = static_cast<int>(sizeof(T));
-  int cluster = ctas_per_row > 0 ? ctas_per_row : kAutoCluster;
+  int cluster = ctas_per_row > 0 ? ctas_per_row : (batch < kSmallBatch ? kAutoClusterSmall : kAutoCluster);
   if (ctas_per_row == 0)
     while (cluster > 1 && vocab / cluster < 2048) --cluster;
   const int32_t chunk = slice_elems(vocab, cluster, esz);
