@@ -47,6 +47,7 @@ BATCH, MEDIAN, SIGMA, LO, HI = 256, 1024, 0.8, 16, 8192
 HQ, HKV, D, BS, SLACK = 14, 2, 64, 16, 1.25
 LAYERS = 24  # Qwen2.5-0.5B decoder layers: one decode iteration is 24 layer calls
 METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s); decode tok/s at 1/2/4/8 B200"
+WORKLOAD_SEED = 1000  # context lengths of the decode batch, for the B200 arm and both CPU arms
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
@@ -65,7 +66,7 @@ def rank_lengths(world: int, rank: int) -> np.ndarray:
     ranks in arrival order by ``SequenceDispatcher`` (most free KV blocks
     first).  At one GPU this is the plain 256-sequence batch."""
     from pagedserve_b200.sharding import shard_sequences
-    lens = context_lengths(1000, BATCH * world)
+    lens = context_lengths(WORKLOAD_SEED, BATCH * world)
     if world == 1:
         return lens
     blocks = int(math.ceil(SLACK * np.sum(-(-lens // BS)) / world))
@@ -352,6 +353,214 @@ def run_select(args, device, seed: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# model-level decode: a whole Qwen2.5-0.5B decode iteration (config 3)
+# ---------------------------------------------------------------------------
+MODEL_BATCH, MODEL_MEDIAN, MODEL_SIGMA = 128, 512, 0.8
+EOS_IDS = (151643, 151645)  # Qwen2.5's end-of-text ids
+
+
+def model_context_lengths(seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return np.clip(np.round(rng.lognormal(math.log(MODEL_MEDIAN), MODEL_SIGMA, MODEL_BATCH)), LO, HI).astype(np.int64)
+
+
+def run_model_decode(args, device, seed: int) -> dict:
+    """One decode iteration of random-init Qwen2.5-0.5B (24 layers, bf16) for
+    128 sequences with lognormal(median 512, sigma 0.8) contexts over a
+    shuffled paged pool: pack_step, embedding, 24 x (RMSNorm, fused QKV GEMM,
+    RoPE + KV write, split-K paged decode, o_proj, residual + RMSNorm, fused
+    gate/up GEMM, SiLU * up, down GEMM), final norm, tied lm_head, greedy
+    selection - one captured graph, the serving loop's decode step."""
+    from pagedserve_b200 import ops
+    from pagedserve_b200.model_runner import QwenConfig, QwenWeights
+    from pagedserve_b200.serving import ReplicaEngine, _BIG_REMAINING
+    cfg = QwenConfig()
+    w = QwenWeights.random(cfg, device, torch.bfloat16, seed=seed)
+    lens = model_context_lengths(seed)
+    rng = np.random.default_rng(seed + 1)
+    need = int(np.sum(-(-(lens + 1) // BS))) + 8
+    nb = int(math.ceil(SLACK * need))
+    eng = ReplicaEngine(w, nb, max_running=MODEL_BATCH, max_prefill_tokens=512, max_prompt=512,
+                        decode_buckets=(MODEL_BATCH,), prefill_buckets=(512,), free_order=rng.permutation(nb))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    eng.cache.kv_cache.k_cache.normal_(generator=gen)
+    eng.cache.kv_cache.v_cache.normal_(generator=gen)
+    ids = [f"m{i}" for i in range(MODEL_BATCH)]
+    for rid, n in zip(ids, lens):
+        eng.cache.allocate(rid, int(n) + 1)
+    eng._upload_tables(ids)
+    rows = np.array([eng._store_row(r) for r in ids], dtype=np.int32)
+    rows_t = torch.from_numpy(rows.astype(np.int64)).to(device)
+    eng.remaining[rows_t] = _BIG_REMAINING
+    eng.last_token[rows_t] = torch.randint(0, cfg.vocab, (MODEL_BATCH,), generator=gen, device=device)
+    g = eng._decode[MODEL_BATCH]
+    eng.capture(decode=True, prefill=False)
+    p = g.plan_host.numpy()
+    p[0], p[1], p[2] = rows, lens - 1, 1  # the token at position ctx - 1 attends over ctx tokens
+    g.plan.copy_(g.plan_host)
+    torch.cuda.synchronize()
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    iters = max(args.steps, 20)
+    it_ms = timed(g.graph.replay, iters)
+    eng.check_errors()
+    # the attention alone, same shapes and metadata: RoPE + KV write and
+    # split-K decode of every layer
+    cu, ctx, slots, pos, tables = g.meta
+    qkv = torch.randn(MODEL_BATCH, cfg.qkv_width, device=device, generator=gen).to(torch.bfloat16)
+    cos, sin = eng.runner.cos.index_select(0, pos), eng.runner.sin.index_select(0, pos)
+    kc, vc = eng.cache.kv_cache.k_cache, eng.cache.kv_cache.v_cache
+    hq, hkv, d = cfg.q_heads, cfg.kv_heads, cfg.head_dim
+    q = qkv[:, :hq * d].view(-1, hq, d)
+    k = qkv[:, hq * d:(hq + hkv) * d].view(-1, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].view(-1, hkv, d)
+    q_rot = torch.empty_like(q)
+    out = torch.empty_like(q)
+
+    def attention():
+        for layer in range(cfg.layers):
+            ops.rope_reshape_and_cache(q, k, v, cos, sin, kc, vc, slots, layer, query_out=q_rot, key_out=False)
+            ops.paged_decode(q_rot, kc, vc, tables, ctx, layer, out=out, max_context=eng.table_width * BS)
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        attention()
+        torch.cuda.synchronize()
+        ga = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga, stream=stream):
+            attention()
+    attn_ms = timed(ga.replay, iters)
+    ga.reset()
+    eng.release()
+    kv_bytes = cfg.layers * decode_bytes(lens)
+    step_bytes = cfg.weight_bytes() + kv_bytes
+    peak, kind = load_peaks()
+    gbs = step_bytes / (it_ms * 1e-3) / 1e9
+    return {
+        "workload": "random-init Qwen2.5-0.5B (24 layers, hidden 896, 14q/2kv, d64, SwiGLU 4864, vocab 151936 tied, "
+                    "QKV bias, bf16), 128 sequences, contexts lognormal(median 512, sigma 0.8) clipped [16, 8192], "
+                    "shuffled block-16 pool, greedy selection; one step = one captured decode iteration",
+        "sequences": MODEL_BATCH, "sum_ctx": int(lens.sum()), "iterations": iters,
+        "ms_per_iteration": round(it_ms, 4), "tok_s": round(MODEL_BATCH / (it_ms * 1e-3), 1),
+        "attention_ms": round(attn_ms, 4), "attention_share": round(attn_ms / it_ms, 4),
+        "weight_mbytes": round(cfg.weight_bytes() / 1e6, 1), "kv_mbytes": round(kv_bytes / 1e6, 1),
+        "gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": kind, "frac": round(gbs / peak, 4),
+        "gpu_launches_per_iteration": "pack_step, 3 gathers, 24 x (2 norms, 4 GEMMs, RoPE+write, decode, combine, "
+                                      "SiLU*up), lm_head, select, 4 index copies",
+    }
+
+
+# ---------------------------------------------------------------------------
+# serving trace: continuous batching, one replica per GPU (config 5)
+# ---------------------------------------------------------------------------
+SERVE_SEED = 5000
+SERVE_RATE_PER_GPU = 3000.0   # arrivals per second per GPU: above what a GPU serves, so the queue never drains
+SERVE_WARMUP_STEPS = 150
+
+
+def run_serving(args, device, world: int, rank: int, group) -> dict:
+    """Continuous batching of a Poisson trace, sequence-sharded: the trace's
+    requests are placed on the ranks at arrival by ``SequenceDispatcher``
+    (fewest reserved tokens, as the free-block rule over a budget that a trace
+    never releases), and each rank serves its share with its own replica,
+    pool and loop (``ReplicaEngine``: FIFO admission with KV reservations,
+    packed prefill, batched decode, greedy selection on the device).  Each
+    rank times ``--serve-steps`` engine steps after SERVE_WARMUP_STEPS."""
+    from pagedserve_b200.model_runner import QwenConfig, QwenWeights
+    from pagedserve_b200.serving import ReplicaEngine, ServeRequest, poisson_trace, prompt_tokens
+    from pagedserve_b200.sharding import SequenceDispatcher, gather_counters
+    cfg = QwenConfig()
+    w = QwenWeights.random(cfg, device, torch.bfloat16, seed=SERVE_SEED)  # the same replica on every rank
+    torch.cuda.empty_cache()
+    free, _ = torch.cuda.mem_get_info(device)
+    block_bytes = cfg.layers * 2 * cfg.kv_heads * BS * cfg.head_dim * 2
+    pool_bytes = min(args.serve_pool_gb * 1e9, free - 24e9)
+    nb = int(pool_bytes // block_bytes)
+    eng = ReplicaEngine(w, nb, max_running=256, eos_ids=EOS_IDS)
+    eng.capture()
+    steps = args.serve_steps
+    per_rank = 256 + 2 * (SERVE_WARMUP_STEPS + steps)
+    trace = poisson_trace(per_rank * world, SERVE_RATE_PER_GPU * world, seed=SERVE_SEED)
+    disp = SequenceDispatcher(world, 1 << 50, BS)
+    mine = [(i, a, p, o) for i, (a, p, o) in enumerate(trace) if disp.assign(str(i), p + o) == rank]
+    nxt = 0
+    t0 = time.perf_counter()
+
+    def pump():
+        nonlocal nxt
+        now = time.perf_counter() - t0
+        while nxt < len(mine) and mine[nxt][1] <= now:
+            i, a, p, o = mine[nxt]
+            eng.submit(ServeRequest(f"t{i}", prompt_tokens(i, p, cfg.vocab, SERVE_SEED), o, arrival=a))
+            nxt += 1
+
+    for _ in range(SERVE_WARMUP_STEPS):
+        pump()
+        eng.step()
+    before = dict(eng.stats)
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier(group=group)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    running = 0
+    for _ in range(steps):
+        pump()
+        eng.step()
+        running += len(eng.scheduler.running)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier(group=group)
+    eng.check_errors()
+    d = {k: eng.stats[k] - before[k] for k in eng.stats}
+    tokens = d["decode_tokens"] + d["first_tokens"]
+    mine_stats = {"ms": ms, "tokens": tokens, "decode_tokens": d["decode_tokens"],
+                  "first_tokens": d["first_tokens"], "prefill_tokens": d["prefill_tokens"],
+                  "finished": d["finished"], "mean_running": running / steps,
+                  "queue_left": len(mine) - nxt + len(eng.scheduler.waiting)}
+    per = gather_counters(mine_stats, group)
+    eng.release()
+    del eng
+    torch.cuda.empty_cache()
+    max_ms = max(r["ms"] for r in per)
+    total = sum(r["tokens"] for r in per)
+    return {
+        "workload": "continuous batching of a Poisson trace (arrivals above service rate), prompts "
+                    "lognormal(median 512, sigma 1.0) clipped [16, 8192], outputs geometric(mean 256), contexts "
+                    "<= 32768; random-init Qwen2.5-0.5B bf16 replicated per GPU; requests placed on GPUs at arrival "
+                    "(SequenceDispatcher); per GPU: FIFO admission with prompt + max_new KV reservations, <= 256 "
+                    "running, <= 16384 prefill tokens per step packed into one prefill, one batched decode per step, "
+                    "greedy selection + EOS/limit test on the device",
+        "pool_gb_per_gpu": round(nb * block_bytes / 1e9, 1), "steps_per_rank": steps,
+        "decode_tok_s": round(total / (max_ms * 1e-3), 1),
+        "decode_only_tok_s": round(sum(r["decode_tokens"] for r in per) / (max_ms * 1e-3), 1),
+        "ms_per_step": round(max_ms / steps, 4),
+        "timing": "CUDA events around each rank's timed steps (one host sync per step, so the span includes the "
+                  "host loop); aggregate = tokens of all ranks / slowest rank's span",
+        "per_rank": [{"tok_s": round(r["tokens"] / (r["ms"] * 1e-3), 1), "ms_per_step": round(r["ms"] / steps, 4),
+                      "tokens": int(r["tokens"]), "prefill_tokens": int(r["prefill_tokens"]),
+                      "finished": int(r["finished"]), "mean_running": round(r["mean_running"], 1),
+                      "queue_left": int(r["queue_left"])} for r in per],
+    }
+
+
+# ---------------------------------------------------------------------------
 # distributed plumbing
 # ---------------------------------------------------------------------------
 def dist_env():
@@ -421,9 +630,11 @@ class Clocks:
 # CPU baseline: the oracle (CPU restatement of the reference's algorithm)
 # ---------------------------------------------------------------------------
 def cpu_oracle_workload(seed: int):
+    """The B200 arm's rank-0 decode batch at one GPU (the same 256 context
+    lengths, pool size and geometry), with seeded numpy K/V/Q values."""
     from oracle import paged_attention as ora
     rng = np.random.default_rng(seed + 7)
-    lens = context_lengths(seed)
+    lens = rank_lengths(1, 0)
     need = int(np.sum(-(-lens // BS)))
     nb = int(math.ceil(SLACK * need))
     perm = rng.permutation(nb)
@@ -435,16 +646,22 @@ def cpu_oracle_workload(seed: int):
     kc = ora.bf16_round(rng.standard_normal((1, nb, HKV, BS, D), dtype=np.float32))
     vc = ora.bf16_round(rng.standard_normal((1, nb, HKV, BS, D), dtype=np.float32))
     q = ora.bf16_round(rng.standard_normal((BATCH, HQ, D), dtype=np.float32))
-    return lens, tables, kc, vc, q
+    new_k = ora.bf16_round(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
+    new_v = ora.bf16_round(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
+    slots = ora.slot_mapping(tables, [int(n) - 1 for n in lens], BS)
+    return lens, tables, kc, vc, q, new_k, new_v, slots
 
 
 def cpu_oracle_call(work, threads: int) -> float:
-    """One full 256-sequence decode layer call of the oracle; returns seconds."""
+    """One full 256-sequence decode step of the oracle - each row's new token
+    written at its last position, then decode attention over the batch (the
+    B200 arm's fused step); returns seconds."""
     from concurrent.futures import ThreadPoolExecutor
     from oracle import paged_attention as ora
-    lens, tables, kc, vc, q = work
+    lens, tables, kc, vc, q, new_k, new_v, slots = work
     parts = np.array_split(np.arange(BATCH), threads)
     t0 = time.perf_counter()
+    ora.reshape_and_cache(new_k, new_v, kc, vc, slots, 0)
     with ThreadPoolExecutor(threads) as ex:
         list(ex.map(lambda idx: ora.decode_attention(q[idx], kc, vc, [tables[i] for i in idx], lens[idx], 0),
                     [p for p in parts if len(p)]))
@@ -454,22 +671,43 @@ def cpu_oracle_call(work, threads: int) -> float:
 def cpu_baseline(seed: int, min_seconds: float = 10.0) -> dict:
     threads = os.cpu_count() or 1
     work = cpu_oracle_workload(seed)
-    nbytes = decode_bytes(work[0])
+    nbytes = decode_bytes(work[0]) + reshape_bytes(BATCH)
     total, calls = 0.0, 0
     while total < min_seconds and calls < 200:
         total += cpu_oracle_call(work, threads)
         calls += 1
     return {"value": round(nbytes * calls / total / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{calls} full 256-sequence decode layer calls of the numpy oracle (reference algorithm "
-                      f"restated), {total:.1f} s, {threads} threads"}
+            "sample": f"{calls} full 256-sequence decode steps (new-token write + decode attention) of the numpy "
+                      f"oracle (the reference algorithm restated) on the B200 arm's rank-0 context lengths, "
+                      f"{total:.1f} s, {threads} threads"}
+
+
+def workload_config(world: int) -> dict:
+    """The headline workload at ``world`` GPUs, from the seeded draws alone
+    (both arms report it)."""
+    shards = [rank_lengths(world, r) for r in range(world)]
+    return {
+        "workload": "serving-scale paged decode + reshape_and_cache: 256 x N_gpus requests, ctx lognormal(median "
+                    "1024, sigma 0.8) clipped [16, 8192], placed on the GPUs in arrival order by most free KV "
+                    "blocks; 14q/2kv heads, d64, block 16, pool 1.25x need per GPU, shuffled blocks",
+        "layers": LAYERS, "sequences": int(sum(len(x) for x in shards)),
+        "sum_ctx": int(sum(int(x.sum()) for x in shards)),
+        "bytes_per_step": int(sum(decode_bytes(x) + reshape_bytes(len(x)) for x in shards)),
+        "l2": f"inputs larger than L2: a {LAYERS}-layer pool, consecutive steps are consecutive layers (~180 MB of "
+              "KV each, read with an evict-first L2 policy)",
+        "launch": f"one CUDA graph per decode iteration: {LAYERS} layer calls, each the fused decode step (new token "
+                  "stored through the block table + split-K attention, then the combine), chained by programmatic "
+                  "dependent launch; a step is one layer call",
+        "parallelism": f"sequence-sharded x{world}",
+    }
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    work = cpu_oracle_workload(0)
-    nbytes = decode_bytes(work[0])
+    work = cpu_oracle_workload(WORKLOAD_SEED)
+    nbytes = decode_bytes(work[0]) + reshape_bytes(BATCH)
     for _ in range(args.warmup):
         cpu_oracle_call(work, threads)
     t = sum(cpu_oracle_call(work, threads) for _ in range(args.steps))
@@ -479,10 +717,11 @@ def run_reference(args, world, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * t / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 values, f64 math",
         "data": "synthetic (seeded)",
-        "config": {"workload": "serving-scale paged decode, 256 seqs, ctx lognormal(1024, 0.8) in [16, 8192], "
-                               "14q/2kv, d64, block 16", "host_threads": threads},
+        "config": workload_config(world),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": "one full 256-sequence decode layer call per step, numpy oracle"},
+                         "sample": "per step one full decode step (new-token write + decode attention) over rank "
+                                   "0's 256 sequences (the B200 arm's context lengths at one GPU), numpy oracle "
+                                   f"(the reference algorithm restated), {threads} host threads"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -522,15 +761,20 @@ def run_b200(args, world, rank, local):
     from pagedserve_b200 import ops, paged_decode_attention_with_write
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    pg = None
+    pg, host_group = None, None
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # The launcher's process group (NCCL, one rank per GPU) carries no
+        # traffic: nothing on the data path crosses GPUs.  Barriers and the
+        # end-of-run counters go over a gloo group on host tensors.
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
         pg = dist
+    sections = set(args.sections.split(","))
 
     LAYERS = args.layers
-    w = build_device_workload(1000 + rank, device, rank_lengths(world, rank), LAYERS)
+    w = build_device_workload(WORKLOAD_SEED + rank, device, rank_lengths(world, rank), LAYERS)
     batch = len(w["lens"])
     k, v = w["cache"].kv_cache.k_cache, w["cache"].kv_cache.v_cache
     out = torch.empty_like(w["q"])
@@ -583,16 +827,21 @@ def run_b200(args, world, rank, local):
         if g_part is not None:
             g_part.replay()
 
-    for _ in range(-(-args.warmup // LAYERS)):  # at least W warm-up layer calls of each kind
-        for g_all, _ in graphs.values():
+    # Warm every graph the timed region replays, the partial graph of the
+    # first K % 24 layers included (its first replay uploads it): at least W
+    # warm-up layer calls of each kind.
+    for _ in range(-(-args.warmup // LAYERS)):
+        for g_all, g_part in graphs.values():
             g_all.replay()
+            if g_part is not None:
+                g_part.replay()
     for g in g_single:
         g.replay()
     torch.cuda.synchronize()
 
     def barrier():
         if pg is not None:
-            pg.barrier()
+            pg.barrier(group=host_group)
 
     def timed(fn):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -694,49 +943,46 @@ def run_b200(args, world, rank, local):
     h2d = in_host.numel() + meta_bytes * iterations / args.steps
     d2h = o_host[0].numel() * 2
 
-    # ---- packed prefill (one engine iteration's attention and KV write) ------
-    prefill = run_prefill(args, device, 2000 + rank)
-    select = run_select(args, device, 3000 + rank)
-
-    # ---- reduce over ranks: times by max, work by sum ------------------------
-    from pagedserve_b200.sharding import aggregate_counters
+    # ---- reduce over ranks (gloo, host tensors): times by max, work by sum ----
+    from pagedserve_b200.sharding import gather_counters
     lens = w["lens"]
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
     rank_step_ms = step_ms
-    times = aggregate_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
-                                "two_ms": two_ms}, device, op="max")
-    work = aggregate_counters({"bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())}, device, op="sum")
-    step_ms, dec_ms, e2e_ms, single_ms = times["step_ms"], times["dec_ms"], times["e2e_ms"], times["single_ms"]
-    two_ms = times["two_ms"]
-    total_bytes, total_seqs = work["bytes"], int(work["seqs"])
+    per_rank = gather_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
+                                "two_ms": two_ms, "bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())},
+                               host_group)
+    step_ms, dec_ms, e2e_ms, single_ms, two_ms = (max(r[k] for r in per_rank) for k in
+                                                 ("step_ms", "dec_ms", "e2e_ms", "single_ms", "two_ms"))
+    total_bytes, total_seqs = sum(r["bytes"] for r in per_rank), int(sum(r["seqs"] for r in per_rank))
+    del w, graphs, g_single, in_dev, o_keep
+    torch.cuda.empty_cache()
+
+    # ---- the other sections (each rank on its own GPU) ----------------------
+    prefill = run_prefill(args, device, 2000 + rank) if "prefill" in sections else None
+    select = run_select(args, device, 3000 + rank) if "select" in sections else None
+    model = run_model_decode(args, device, 4000) if "model" in sections else None
+    torch.cuda.empty_cache()
+    serving = run_serving(args, device, world, rank, host_group) if "serve" in sections else None
     value = total_bytes / (step_ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
     achieved = step_bytes / (rank_step_ms * 1e-3) / 1e9
 
     if rank == 0:
-        cpu = cpu_baseline(0) if world == 1 else None
+        cpu = cpu_baseline(WORKLOAD_SEED) if world == 1 else None
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) KV/Q, lognormal contexts)",
-            "config": {"layers": LAYERS,
-                       "workload": "serving-scale paged decode + reshape_and_cache: 256 x N_gpus requests, ctx "
-                                   "lognormal(median 1024, sigma 0.8) clipped [16, 8192], placed on the GPUs in "
-                                   "arrival order by most free KV blocks; 14q/2kv heads, d64, block 16, pool 1.25x "
-                                   "need per GPU, shuffled blocks",
-                       "sequences": total_seqs, "sum_ctx": int(work["ctx"]), "bytes_per_step": int(total_bytes),
-                       "rank0_sequences": batch, "rank0_sum_ctx": int(lens.sum()),
-                       "l2": f"inputs larger than L2: a {LAYERS}-layer pool, consecutive steps are consecutive "
-                             "layers (~180 MB of KV each, read with an evict-first L2 policy)",
-                       "launch": f"one CUDA graph per decode iteration: {LAYERS} layer calls, each the fused decode "
-                                 "step (new token stored through the block table + split-K attention, then the "
-                                 "combine), chained by programmatic dependent launch; a step is one layer call",
-                       "per_layer_graph_ms": round(single_ms, 5),
-                       "per_layer_graph_note": "the same layer calls launched as one CUDA graph each",
-                       "two_launch_ms": round(two_ms, 5),
-                       "two_launch_note": "the step as reshape_and_cache (slot mapping) then decode, same graphs",
-                       "parallelism": f"sequence-sharded x{world}"},
+            "config": workload_config(world),
+            "detail": {
+                "per_layer_graph_ms": round(single_ms, 5),
+                "per_layer_graph_note": "the same layer calls launched as one CUDA graph each",
+                "two_launch_ms": round(two_ms, 5),
+                "two_launch_note": "the step as reshape_and_cache (slot mapping) then decode, same graphs",
+                "per_rank": [{"step_ms": round(r["step_ms"], 5), "sequences": int(r["seqs"]), "sum_ctx": int(r["ctx"]),
+                              "gbs": round(r["bytes"] / (r["step_ms"] * 1e-3) / 1e9, 1)} for r in per_rank],
+            },
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
             "attn_layer_tok_per_s": round(total_seqs / (step_ms * 1e-3), 1),
@@ -748,8 +994,8 @@ def run_b200(args, world, rank, local):
                          "bytes_per_launch": step_bytes,
                          "avg_launch_ms": round(rank_step_ms, 5), "traffic": STEP_TRAFFIC_BYTES,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused decode "
-                                           "(187.5 + 4.3 MB) and one combine (6.0 MB) launch on this seeded "
-                                           "workload (decode ncu summary under profiles/)",
+                                           "and one combine launch on this seeded workload (decode ncu summary "
+                                           "under profiles/)",
                          "decode_only_ms": round(dec_ms, 5),
                          "decode_only_note": "decode + combine without the new-token store, same graphs"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
@@ -762,15 +1008,14 @@ def run_b200(args, world, rank, local):
             "gpu_launches": 2 * args.steps,
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
             "clocks": clocks.summary(),
+            "decode": model,
+            "serving": serving,
             "prefill": prefill,
             "select_tokens": select,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    for g in [g for pair in graphs.values() for g in pair] + g_single:
-        if g is not None:
-            g.reset()
     if pg is not None:
         pg.destroy_process_group()
 
@@ -781,6 +1026,12 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--serve-steps", type=int, default=600,
+                    help="engine steps each rank times in the serving trace")
+    ap.add_argument("--serve-pool-gb", type=float, default=150.0,
+                    help="KV pool per GPU for the serving trace (capped by free memory)")
+    ap.add_argument("--sections", default="decode,prefill,select,model,serve",
+                    help="comma-separated sections besides the headline decode step")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layers in the pool and the iteration graph (default: the model's 24); every step is "
                          "still one full layer call, so fewer only shrink the device memory a profiler must "

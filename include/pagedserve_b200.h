@@ -101,9 +101,10 @@ int psb_reshape_and_cache(const void* key, int64_t key_stride_t, int64_t key_str
 size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads, int32_t num_kv_heads, int32_t head_dim,
                                        int32_t block_size, int32_t max_context, int32_t dtype);
 
-/* Zero the counter region of a workspace (async memset on ``stream``).  Kept
- * for callers written against earlier versions; psb_paged_decode no longer
- * needs it. */
+/* Zero the arrival-counter region of a workspace (async memset on
+ * ``stream``).  Optional: psb_paged_decode clears what it relies on itself;
+ * this is for callers that want a freshly allocated workspace in a known
+ * state before its first use. */
 int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int32_t batch, int32_t num_kv_heads,
                                     psb_stream_t stream);
 
@@ -202,17 +203,21 @@ int psb_paged_decode_append(const void* query, int64_t q_stride_b, int64_t q_str
  *
  * The split-K scratch is a file-scope device array of
  * psb_paged_decode_static_capacity() bytes (32 MiB) per device, reserved when
- * its module loads; the call allocates nothing.  A geometry whose
- * psb_paged_decode_workspace_size(...) exceeds that returns
- * PSB_ERR_WORKSPACE (e.g. 64 sequences of up to 4096 tokens fit, 256 of up
- * to 8192 do not).
+ * its module loads; the call allocates nothing.  Only the scratch of the path
+ * the call takes is checked against that: the bf16/f16 head_dim-64 path needs
+ * a fixed ~10.8 MB whatever the batch (256 sequences of up to 8192 tokens
+ * fit); the CUDA-core path needs per-chunk partials that grow with batch x
+ * max_context, and a call whose need exceeds the array returns
+ * PSB_ERR_WORKSPACE.
  *
  * Set-up: the first call on each device looks up the array's address with
  * that device current (and may load the module); make that first call before
- * any stream capture.  Every call clears the scratch's counter region with an
- * async memset on ``stream`` and then launches decode there.  The scratch is
- * shared by every caller on a device: calls that overlap on the GPU (other
- * streams, other threads) race and must be serialised by the caller.
+ * any stream capture.  Decode clears what it relies on itself (the CUDA-core
+ * path zeroes its arrival counters at the start of every call; the fast
+ * path's partial slots are written before they are read).  The scratch is
+ * shared by every caller on a device and keeps the last call's contents:
+ * calls that overlap on the GPU (other streams, other threads) race and must
+ * be serialised by the caller.
  * Arguments, results and error behaviour are otherwise psb_paged_decode's.
  */
 int psb_paged_decode_static(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
@@ -323,6 +328,32 @@ int psb_pack_step(const int32_t* table_store, int64_t store_width, int32_t store
                   const int32_t* starts, const int32_t* query_lens, int32_t batch, int32_t total, int32_t block_size,
                   int32_t* cu_seqlens, int32_t* context_lens, int64_t* slot_mapping, int64_t* positions,
                   int32_t* block_tables, int32_t out_width, int32_t* error_flag, psb_stream_t stream);
+
+/*
+ * add_rms_norm: a Qwen2 decoder layer's residual add fused with RMSNorm.
+ *
+ * Replaces ``residual + x`` followed by Qwen2RMSNorm (transformers' module,
+ * called by the reference's model runner at pagedserve/model/engine.py:577-598
+ * for decode and :628-648 for prefill).  With ``residual`` non-null, for every
+ * row: residual = round(residual + x) (in place), out = RMSNorm(residual);
+ * with ``residual`` null, out = RMSNorm(x).  RMSNorm(r) = round(weight *
+ * round(r * rsqrt(mean(r^2) + eps))), the mean over ``hidden`` in fp32.
+ * x, residual, out are [rows, hidden] with row strides in elements and unit
+ * element stride; weight is [hidden]; all of ``dtype``.
+ */
+int psb_add_rms_norm(const void* x, int64_t x_stride, void* residual, int64_t residual_stride, const void* weight,
+                     void* out, int64_t out_stride, int32_t rows, int32_t hidden, float eps, int32_t dtype,
+                     psb_stream_t stream);
+
+/*
+ * silu_and_mul: the Qwen2 MLP's activation, act_fn(gate_proj(x)) * up_proj(x)
+ * (transformers' Qwen2MLP, called at pagedserve/model/engine.py:595 and :645),
+ * over a fused [rows, 2 * intermediate] gate|up projection:
+ *     out[r, j] = round(round(silu(gate_up[r, j])) * gate_up[r, intermediate + j])
+ * silu evaluated in fp32.  Row strides in elements, unit element stride.
+ */
+int psb_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride, int32_t rows,
+                     int32_t intermediate, int32_t dtype, psb_stream_t stream);
 
 /* Number of SMs of the current device (for callers sizing persistent grids). */
 int psb_device_sm_count(void);

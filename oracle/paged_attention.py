@@ -16,9 +16,9 @@ against those vectors.
 Reference functions restated (paths inside the PagedServe project):
 
 * ``decode_attention``   <- pagedserve/attention/vectorized_batched_attention.py:79-159
-* ``causal_attention``   <- pagedserve/attention/paged_attention.py:239-305 (lines 94-145
-                            of the function body: per-position causal gather, fp32 softmax,
-                            probabilities cast to the query dtype before P.V)
+* ``causal_attention``   <- pagedserve/attention/paged_attention.py:94-145 (per-position causal
+                            gather, fp32 softmax, probabilities cast to the query dtype
+                            before P.V at :133-137)
 * ``write_tokens``       <- pagedserve/engine/paged_kv_cache.py:187-200
 * ``slot_for``           <- pagedserve/engine/paged_kv_cache.py:187-192
 * ``padded_block_table`` <- pagedserve/attention/triton_paged_decode.py:134-154
@@ -55,6 +55,7 @@ __all__ = [
     "causal_attention",
     "paged_causal_attention",
     "varlen_causal_attention",
+    "varlen_causal_attention_blocked",
     "write_tokens",
     "reshape_and_cache",
     "pack_step",
@@ -223,7 +224,7 @@ def causal_attention(q: np.ndarray, keys: np.ndarray, values: np.ndarray, start:
 
     Query row ``i`` (position ``start + i``) sees keys ``0 .. start + i`` of
     ``keys, values [Hkv, >= start + S, D]``.  Restates paged_attention
-    (paged_attention.py:248-305).
+    (paged_attention.py:94-145).
     """
     hq, s, d = q.shape
     hkv = keys.shape[0]
@@ -253,7 +254,7 @@ def varlen_causal_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seql
 
     Sequence ``i`` owns rows ``cu_seqlens[i] .. cu_seqlens[i+1]`` and is causal
     within itself.  Per sequence this is exactly ``paged_attention`` with
-    ``query_start_position = 0`` (paged_attention.py:253-304), which the
+    ``query_start_position = 0`` (paged_attention.py:94-145), which the
     reference runs one request at a time (qwen_paged_attention.py:110-128).
     """
     t, hq, d = q.shape
@@ -272,6 +273,38 @@ def varlen_causal_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seql
 # --------------------------------------------------------------------------
 # KV scatter
 # --------------------------------------------------------------------------
+
+def varlen_causal_attention_blocked(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_seqlens: Sequence[int],
+                                    rows: int = 256) -> np.ndarray:
+    """``varlen_causal_attention`` in ``mode="exact"`` (float64), evaluated
+    ``rows`` query rows and one kv head at a time as matrix products instead
+    of one row at a time: the same arithmetic (paged_attention.py:94-145 per
+    sequence), fast enough for full 16K-token packs.  Pinned to the per-row
+    form by the oracle tests."""
+    t, hq, d = q.shape
+    hkv = k.shape[1]
+    group = hq // hkv
+    out = np.zeros((t, hq, d), dtype=np.float64)
+    scale = 1.0 / math.sqrt(d)
+    for i in range(len(cu_seqlens) - 1):
+        a, b = int(cu_seqlens[i]), int(cu_seqlens[i + 1])
+        n = b - a
+        for kh in range(hkv):
+            keys = k[a:b, kh].astype(np.float64)          # [n, D]
+            vals = v[a:b, kh].astype(np.float64)
+            heads = slice(kh * group, (kh + 1) * group)
+            for r0 in range(0, n, rows):
+                r1 = min(n, r0 + rows)
+                qq = q[a + r0:a + r1, heads].astype(np.float64)          # [r, G, D]
+                sc = np.einsum("rgd,kd->rgk", qq, keys[:r1]) * scale     # keys 0 .. r1 - 1
+                vis = np.arange(r1)[None, :] <= np.arange(r0, r1)[:, None]  # [r, k] causal
+                sc = np.where(vis[:, None, :], sc, -np.inf)
+                sc -= sc.max(axis=-1, keepdims=True)
+                e = np.exp(sc)
+                p = e / e.sum(axis=-1, keepdims=True)
+                out[a + r0:a + r1, heads] = np.einsum("rgk,kd->rgd", p, vals[:r1])
+    return out
+
 
 def write_tokens(k_cache: np.ndarray, v_cache: np.ndarray, layer: int, table: Sequence[int],
                  positions: Sequence[int], keys: np.ndarray, values: np.ndarray) -> None:

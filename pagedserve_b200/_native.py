@@ -64,6 +64,9 @@ SIGNATURES = {
     "psb_select_tokens": (ctypes.c_int, [
         _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,
         _c_void_p]),
+    "psb_add_rms_norm": (ctypes.c_int, [
+        _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i32, _i32, _f32, _i32, _c_void_p]),
+    "psb_silu_and_mul": (ctypes.c_int, [_c_void_p, _i64, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p]),
     "psb_pack_step": (ctypes.c_int, [
         _c_void_p, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p,
         _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p]),

@@ -36,6 +36,9 @@ from . import ops
 
 _KEEP = 4  # metadata entries kept per cache (one per live batch shape)
 
+# triton_paged_decode.py:106-107 raises exactly this text for a host query
+_CUDA_REQUIRED = "Triton paged attention requires CUDA"
+
 
 def _memo(cache, kind: str, request_ids, positions, device, build):
     """``build()``, or its result from an earlier call at the same cache
@@ -143,7 +146,9 @@ def _validated_metadata(query, cache, request_ids, positions, layer):
     """The reference wrapper's checks, in its order and with its messages
     (triton_paged_decode.py:106-141), then the device table and lengths."""
     if not query.is_cuda:
-        raise ValueError("B200 paged attention requires CUDA")
+        # the reference wrapper's message, word for word: callers that match
+        # on it keep working when this backend replaces the Triton one
+        raise ValueError(_CUDA_REQUIRED)
     if query.ndim != 4 or query.shape[2] != 1:
         raise ValueError("query must have shape [B, Hq, 1, D]")
     if query.dtype not in (torch.float32, torch.float16, torch.bfloat16):
@@ -185,7 +190,7 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     the query attends to.  Runs as ``psb_paged_decode_append``.
     """
     if not query.is_cuda:
-        raise ValueError("B200 paged attention requires CUDA")
+        raise ValueError(_CUDA_REQUIRED)
     kv = cache.kv_cache
     if key.ndim == 4:
         key, value = key.squeeze(2), value.squeeze(2)

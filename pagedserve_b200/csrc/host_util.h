@@ -53,6 +53,16 @@ inline void discard_stale_error() { (void)cudaGetLastError(); }
 
 CUtensorMapDataType dtype_to_tmap(int dtype);
 
+// Scratch bytes one psb_paged_decode call with these arguments needs on the
+// path it will take (fast: the fixed split-K slot table; generic: counters
+// and per-chunk partials), 0 for an invalid geometry.  Unlike
+// psb_paged_decode_workspace_size, which covers either path because it does
+// not see the pointers, this is exact for the call.
+size_t decode_scratch_for_call(const void* query, int64_t q_stride_b, int64_t q_stride_h, const void* out,
+                               int64_t o_stride_b, int64_t o_stride_h, const void* k_cache, const void* v_cache,
+                               int32_t batch, int32_t q_heads, int32_t num_kv_heads, int32_t block_size,
+                               int32_t head_dim, int32_t dtype, int32_t max_context);
+
 // Launch with programmatic stream serialization (the kernel may begin while
 // its stream predecessor is still running; see pdl_wait in common.cuh).
 template <typename... KArgs, typename... Args>

@@ -1234,6 +1234,20 @@ extern "C" size_t psb_paged_decode_workspace_size(int32_t batch, int32_t q_heads
   return std::max(fast, gen);
 }
 
+size_t psb::decode_scratch_for_call(const void* query, int64_t q_stride_b, int64_t q_stride_h, const void* out,
+                                    int64_t o_stride_b, int64_t o_stride_h, const void* k_cache,
+                                    const void* v_cache, int32_t batch, int32_t q_heads, int32_t num_kv_heads,
+                                    int32_t block_size, int32_t head_dim, int32_t dtype, int32_t max_context) {
+  if (batch <= 0 || num_kv_heads <= 0 || q_heads <= 0 || q_heads % num_kv_heads || head_dim <= 0 ||
+      block_size <= 0 || max_context < 0)
+    return 0;
+  const int group = q_heads / num_kv_heads;
+  const int hp = choose_path(dtype, head_dim, block_size, group, num_kv_heads, batch, max_context, query, q_stride_b,
+                             q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache);
+  if (hp) return fast_layout().total;
+  return workspace_layout(split_geometry(batch, num_kv_heads, group, max_context), head_dim).total;
+}
+
 extern "C" int psb_paged_decode_workspace_init(void* workspace, size_t workspace_bytes, int32_t batch,
                                                int32_t num_kv_heads, psb_stream_t stream) {
   if (workspace == nullptr || batch <= 0 || num_kv_heads <= 0) return PSB_ERR_INVALID;

@@ -23,9 +23,11 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(32) << 20;
 constexpr int kMaxDevices = 64;
 
-// Split-K partials, steal state and arrival counters for one call at a time
-// per device.  Zero-initialised at module load; the counter prefix is cleared
-// again before every call.
+// Split-K scratch for one call at a time per device: on the bf16/f16 fast
+// path the fixed table of per-warp partial slots (written before it is read
+// in every call, so it needs no clearing), on the CUDA-core path the
+// per-(sequence, kv head) arrival counters, which that path zeroes itself at
+// the start of every call, and the per-chunk partials.
 __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
 std::mutex g_scratch_mu;
@@ -62,16 +64,17 @@ extern "C" int psb_paged_decode_static(const void* query, int64_t q_stride_b, in
                                        int32_t block_size, int32_t head_dim, int32_t dtype, int32_t max_context,
                                        float scale, int32_t* error_flag, psb_stream_t stream) {
   if (!query || !out || !k_cache || !v_cache || !block_tables || !context_lens) return PSB_ERR_INVALID;
-  const size_t need = psb_paged_decode_workspace_size(batch, q_heads, num_kv_heads, head_dim, block_size,
-                                                      max_context, dtype);
+  // only the scratch of the path this call takes counts: the fast path's is a
+  // fixed ~10.8 MB whatever the batch, so serving batches fit that the
+  // CUDA-core path's per-chunk partials would not
+  const size_t need = psb::decode_scratch_for_call(query, q_stride_b, q_stride_h, out, o_stride_b, o_stride_h,
+                                                   k_cache, v_cache, batch, q_heads, num_kv_heads, block_size,
+                                                   head_dim, dtype, max_context);
   if (need == 0) return PSB_ERR_INVALID;
   if (need > kStaticScratchBytes) return PSB_ERR_WORKSPACE;
   void* scratch = nullptr;
   const int st = scratch_for_current_device(&scratch);
   if (st != PSB_OK) return st;
-  // The work queue and arrival counters must read zero when decode starts.
-  const int init = psb_paged_decode_workspace_init(scratch, kStaticScratchBytes, batch, num_kv_heads, stream);
-  if (init != PSB_OK) return init;
   return psb_paged_decode(query, q_stride_b, q_stride_h, out, o_stride_b, o_stride_h, k_cache, v_cache,
                           block_tables, table_stride, context_lens, batch, q_heads, layer, num_layers, num_blocks,
                           num_kv_heads, block_size, head_dim, dtype, max_context, scale, scratch,

@@ -320,7 +320,10 @@ __global__ void __launch_bounds__(kSelThreads) select_stream_kernel(
     const bool got = __all_sync(0xFFFFFFFFu, mbar_wait(&full[warp][slot], static_cast<uint32_t>((j / kSlots) & 1)));
     if (!got) {
       if (lane == 0) flag_error(err, PSB_DEVERR_TIMEOUT);
-      // the other slots' copies, where issued, land before the CTA may exit
+      // Wait (bounded) for the other slots' copies, where issued.  Slot j's
+      // own copy is the one that timed out and may still be in flight when
+      // the CTA exits; the error flag tells the host that this launch's
+      // results, and the shared memory it leaves, are not to be trusted.
       for (int q = j + 1; q < j + kSlots && q < total; ++q)
         (void)mbar_wait(&full[warp][q % kSlots], static_cast<uint32_t>((q / kSlots) & 1));
       break;

@@ -1,7 +1,7 @@
 // Packed ragged causal prefill attention.
 //
 // Replaces the reference's per-request prefill attention
-// (pagedserve/attention/qwen_paged_attention.py:121-128 -> paged_attention.py:253-304,
+// (pagedserve/attention/qwen_paged_attention.py:121-128 -> paged_attention.py:94-145,
 // O(S^2) Python gathers per request) with one launch over a packed batch:
 // q [T, Hq, D], k/v [T, Hkv, D], sequence i = rows cu_seqlens[i]..cu_seqlens[i+1],
 // causal within each sequence, GQA (q head h reads kv head h / (Hq/Hkv)).
@@ -10,7 +10,7 @@
 // tensor-core kernel (varlen_prefill_tc.cu) does not cover: one warp per
 // (query row, q head), 32 keys per step (one key per lane for Q.K, lanes
 // over head_dim for P.V), online softmax in fp32, probabilities rounded to
-// the input dtype before P.V as paged_attention.py:291-302 does.
+// the input dtype before P.V as paged_attention.py:133-137 does.
 #include <algorithm>
 
 #include "common.cuh"

@@ -2,7 +2,7 @@
 //
 // Replaces the reference's one-request-at-a-time prefill attention
 // (pagedserve/attention/qwen_paged_attention.py:121-128 calling
-// pagedserve/attention/paged_attention.py:239-305) for bf16/f16, head_dim 64:
+// pagedserve/attention/paged_attention.py:94-145) for bf16/f16, head_dim 64:
 // q [T, Hq, 64], k/v [T, Hkv, 64], sequence i = rows cu[i] .. cu[i+1], causal
 // within each sequence, q head h reads kv head h / (Hq / Hkv).
 //
@@ -25,7 +25,7 @@
 //   softmax: thread r loads its row of S, masks keys past its own position or
 //   past the sequence and stores P = exp2(S - m) rounded to the input type
 //   (as the reference rounds the probabilities before P.V,
-//   paged_attention.py:291-302) to its TMEM lane, two keys per column.  m is
+//   paged_attention.py:133-137) to its TMEM lane, two keys per column.  m is
 //   a lazily updated row max: only when a row's max grows by more than 2^8 is
 //   the O accumulated so far in TMEM rescaled (so P stays below 256 and most
 //   steps touch no O at all);

@@ -404,13 +404,15 @@ def paged_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
 
 
 def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.Tensor, query_lens: torch.Tensor,
-              total: int, block_size: int, out_width: int | None = None, error_flag: torch.Tensor | None = None):
+              total: int, block_size: int, out_width: int | None = None, error_flag: torch.Tensor | None = None,
+              out: tuple | None = None):
     """Build one step's ragged-batch metadata on the GPU.
 
     ``table_store [R, W]`` int32 holds every live request's block table (one
     row each); ``req_rows, starts, query_lens [B]`` int32 are the scheduler's
     step plan.  Returns ``(cu_seqlens, context_lens, slot_mapping, positions,
-    block_tables)``.
+    block_tables)``, written into ``out`` (the same five tensors, e.g. the
+    static buffers of a captured step) when given.
     """
     _require_cuda(table_store, req_rows, starts, query_lens)
     for name, x in (("req_rows", req_rows), ("starts", starts), ("query_lens", query_lens)):
@@ -421,11 +423,21 @@ def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.T
     bsz = req_rows.shape[0]
     out_width = table_store.shape[1] if out_width is None else int(out_width)
     dev = table_store.device
-    cu = torch.empty(bsz + 1, dtype=torch.int32, device=dev)
-    ctx = torch.empty(bsz, dtype=torch.int32, device=dev)
-    slots = torch.empty(total, dtype=torch.int64, device=dev)
-    pos = torch.empty(total, dtype=torch.int64, device=dev)
-    tables = torch.empty((bsz, out_width), dtype=torch.int32, device=dev)
+    if out is None:
+        cu = torch.empty(bsz + 1, dtype=torch.int32, device=dev)
+        ctx = torch.empty(bsz, dtype=torch.int32, device=dev)
+        slots = torch.empty(total, dtype=torch.int64, device=dev)
+        pos = torch.empty(total, dtype=torch.int64, device=dev)
+        tables = torch.empty((bsz, out_width), dtype=torch.int32, device=dev)
+    else:
+        cu, ctx, slots, pos, tables = out
+        ok = (cu.shape == (bsz + 1,) and cu.dtype == torch.int32 and ctx.shape == (bsz,) and ctx.dtype == torch.int32
+              and slots.shape == (total,) and slots.dtype == torch.int64 and pos.shape == (total,)
+              and pos.dtype == torch.int64 and tables.shape == (bsz, out_width) and tables.dtype == torch.int32
+              and all(t.is_contiguous() for t in out))
+        if not ok:
+            raise ValueError("out must be contiguous (cu_seqlens [B+1] i32, context_lens [B] i32, slot_mapping [T] "
+                             "i64, positions [T] i64, block_tables [B, out_width] i32)")
     lib = _native.load()
     _native.check(lib.psb_pack_step(
         table_store.data_ptr(), table_store.stride(0), table_store.shape[0], req_rows.contiguous().data_ptr(),
@@ -433,6 +445,47 @@ def pack_step(table_store: torch.Tensor, req_rows: torch.Tensor, starts: torch.T
         cu.data_ptr(), ctx.data_ptr(), slots.data_ptr(), pos.data_ptr(), tables.data_ptr(), out_width,
         _ptr(error_flag), _stream(dev)), "pack_step")
     return cu, ctx, slots, pos, tables
+
+
+def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of ``x [R, H]`` (Qwen2RMSNorm), or, with ``residual [R, H]``,
+    ``residual += x`` (rounded, in place) followed by RMSNorm of the sum, in
+    one launch (psb_add_rms_norm).  Returns ``out``."""
+    _require_cuda(x, weight)
+    if x.ndim != 2 or weight.shape != (x.shape[1],):
+        raise ValueError("x must be [R, H] and weight [H]")
+    if x.stride(1) != 1 or weight.stride(0) != 1:
+        raise ValueError("x and weight need unit stride along H")
+    if out is None:
+        out = torch.empty_like(x)
+    for t in (out,) + ((residual,) if residual is not None else ()):
+        if t.shape != x.shape or t.dtype != x.dtype or t.stride(1) != 1:
+            raise ValueError("out / residual must match x's shape and dtype with unit stride along H")
+    if weight.dtype != x.dtype:
+        raise ValueError("weight dtype must match x")
+    lib = _native.load()
+    _native.check(lib.psb_add_rms_norm(
+        x.data_ptr(), x.stride(0), _ptr(residual), residual.stride(0) if residual is not None else 0,
+        weight.data_ptr(), out.data_ptr(), out.stride(0), x.shape[0], x.shape[1], float(eps), dtype_code(x.dtype),
+        _stream(x.device)), "add_rms_norm")
+    return out
+
+
+def silu_and_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate) * up`` of a fused ``gate_up [R, 2I]`` projection -> ``[R, I]`` (psb_silu_and_mul)."""
+    _require_cuda(gate_up)
+    if gate_up.ndim != 2 or gate_up.shape[1] % 2 or gate_up.stride(1) != 1:
+        raise ValueError("gate_up must be [R, 2 * I] with unit column stride")
+    rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty((rows, inter), dtype=gate_up.dtype, device=gate_up.device)
+    if out.shape != (rows, inter) or out.dtype != gate_up.dtype or out.stride(1) != 1:
+        raise ValueError(f"out must be [{rows}, {inter}] of gate_up's dtype with unit column stride")
+    lib = _native.load()
+    _native.check(lib.psb_silu_and_mul(gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(), out.stride(0), rows,
+                                       inter, dtype_code(gate_up.dtype), _stream(gate_up.device)), "silu_and_mul")
+    return out
 
 
 SELECT_DONE, SELECT_EOS, SELECT_LIMIT = 1, 2, 4

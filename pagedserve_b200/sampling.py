@@ -80,11 +80,33 @@ def _staging(n: int) -> tuple[torch.Tensor, torch.Tensor]:
     return bufs[0][:n], bufs[1][:n]
 
 
+class GenerationLimitError(RuntimeError):
+    """A row of the batch had no tokens left to generate.
+
+    The reference's ``Request.add_generated_token`` raises ``RuntimeError``
+    with this message (request.py:105-106) inside its per-row loop
+    (continuous_batcher.py:333-360), after the rows before the failing one
+    have taken their tokens.  ``row`` is the first such row; ``tokens`` and
+    ``finished`` hold the whole batch's selection, so a caller can apply rows
+    ``0 .. row - 1`` as the reference does.  On the device, ``remaining`` has
+    already been decremented for every row that was not at its limit (rows
+    at their limit keep their counter).
+    """
+
+    def __init__(self, row: int, tokens: list[int], finished: list[bool]):
+        super().__init__("Request has reached its generation limit")
+        self.row = row
+        self.tokens = tokens
+        self.finished = finished
+
+
 def read_selection(tokens: torch.Tensor, status: torch.Tensor) -> tuple[list[int], list[bool]]:
     """Host copy of one step's selection: (token ids, finished flags).
 
-    One synchronisation for the batch.  Raises ``RuntimeError`` with the
-    reference's message (request.py:105-106) when a row had no tokens left.
+    One synchronisation for the batch.  Raises ``GenerationLimitError`` (a
+    ``RuntimeError`` with the reference's message, request.py:105-106) when a
+    row had no tokens left; it carries the batch's tokens and flags and the
+    first failing row.
     """
     if tokens.numel() != status.numel():
         raise ValueError("tokens and status differ in length")
@@ -93,6 +115,9 @@ def read_selection(tokens: torch.Tensor, status: torch.Tensor) -> tuple[list[int
     host_s.copy_(status.reshape(-1), non_blocking=True)
     torch.cuda.current_stream(tokens.device).synchronize()
     flags = host_s.tolist()
-    if any(f & ops.SELECT_LIMIT for f in flags):
-        raise RuntimeError("Request has reached its generation limit")
-    return host_t.tolist(), [bool(f & ops.SELECT_DONE) for f in flags]
+    ids = host_t.tolist()
+    finished = [bool(f & ops.SELECT_DONE) for f in flags]
+    for row, f in enumerate(flags):
+        if f & ops.SELECT_LIMIT:
+            raise GenerationLimitError(row, ids, finished)
+    return ids, finished

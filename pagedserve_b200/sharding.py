@@ -105,14 +105,14 @@ def shard_sequences(lengths: Sequence[int], world_size: int, blocks_per_rank: in
     return [[int(rid) for rid in d.shard(r)] for r in range(world_size)]
 
 
-def aggregate_counters(counters: dict[str, float], device: torch.device | str = "cpu", op: str = "sum"
-                       ) -> dict[str, float]:
-    """Combine per-rank counters over the default process group.
+def aggregate_counters(counters: dict[str, float], device: torch.device | str = "cpu", op: str = "sum",
+                       group=None) -> dict[str, float]:
+    """Combine per-rank counters over ``group`` (default: the default process group).
 
     ``op`` is ``"sum"`` (tokens served, bytes moved) or ``"max"`` (step time:
     the job is as slow as its slowest rank).  ``device`` is where the staging
-    tensor lives: ``"cpu"`` for gloo, the rank's GPU for NCCL.  Every rank
-    must pass the same keys.  Without an initialised process group the
+    tensor lives: ``"cpu"`` for a gloo group, the rank's GPU for NCCL.  Every
+    rank must pass the same keys.  Without an initialised process group the
     counters come back unchanged.
     """
     import torch.distributed as dist
@@ -122,8 +122,23 @@ def aggregate_counters(counters: dict[str, float], device: torch.device | str = 
     if not (dist.is_available() and dist.is_initialized()):
         return {k: float(counters[k]) for k in keys}
     t = torch.tensor([float(counters[k]) for k in keys], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX, group=group)
     return {k: float(v) for k, v in zip(keys, t.tolist())}
+
+
+def gather_counters(counters: dict[str, float], group=None) -> list[dict[str, float]]:
+    """Every rank's counters, in rank order, over a gloo ``group`` (host
+    tensors).  Every rank must pass the same keys; without an initialised
+    process group this is ``[counters]``."""
+    import torch.distributed as dist
+    keys = sorted(counters)
+    if not (dist.is_available() and dist.is_initialized()):
+        return [{k: float(counters[k]) for k in keys}]
+    world = dist.get_world_size(group)
+    t = torch.tensor([float(counters[k]) for k in keys], dtype=torch.float64)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t, group=group)
+    return [{k: float(v) for k, v in zip(keys, o.tolist())} for o in out]
 
 
 def balanced(shards: Iterable[Sequence[int]], lengths: Sequence[int]) -> list[int]:

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <PagedServe checkout>
 
 For every case in ``cases.py`` it builds the reference's own ``PagedKVCache``
 on the CPU, reproduces the case's block tables with the reference allocator,
@@ -65,7 +65,8 @@ def pool_digest(arr: np.ndarray, dtype: str) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of a PagedServe checkout (the directory holding the pagedserve package)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
 

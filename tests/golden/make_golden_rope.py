@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden_rope.py --reference /root/reference
+    python tests/golden/make_golden_rope.py --reference <PagedServe checkout>
 
 The reference rotates q and k in its decode glue with ``apply_rotary_pos_emb``
 as imported by pagedserve/attention/batched_paged_attention.py:8 (the
@@ -36,7 +36,8 @@ HQ, HKV, D, THETA = 14, 2, 64, 1e6
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of a PagedServe checkout (the directory holding the pagedserve package)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
 

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden_select.py --reference /root/reference
+    python tests/golden/make_golden_select.py --reference <PagedServe checkout>
 
 For seeded [B, S, V] logits (with planted ties, NaNs, infinities, signed
 zeros and all--inf rows) this evaluates the reference's own expression
@@ -56,7 +56,8 @@ def plant(logits, rng):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of a PagedServe checkout (the directory holding the pagedserve package)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
 

@@ -20,11 +20,15 @@ def poison_unused(k_cache: np.ndarray, v_cache: np.ndarray, layer: int, tables, 
     kc = np.full_like(k_cache, np.nan)
     vc = np.full_like(v_cache, np.nan)
     bs = k_cache.shape[3]
+    blks, offs = [], []
     for table, n in zip(tables, lens):
-        for pos in range(int(n)):
-            blk, off = table[pos // bs], pos % bs
-            kc[layer, blk, :, off, :] = k_cache[layer, blk, :, off, :]
-            vc[layer, blk, :, off, :] = v_cache[layer, blk, :, off, :]
+        pos = np.arange(int(n))
+        blks.append(np.asarray(table, dtype=np.int64)[pos // bs])
+        offs.append(pos % bs)
+    if blks:
+        blk, off = np.concatenate(blks), np.concatenate(offs)
+        kc[layer, blk, :, off, :] = k_cache[layer, blk, :, off, :]
+        vc[layer, blk, :, off, :] = v_cache[layer, blk, :, off, :]
     return kc, vc
 
 

@@ -117,9 +117,14 @@ def test_static_decode_checks_need_no_gpu():
     null, fake = None, 256  # never dereferenced: every call below is rejected first
     assert lib.psb_paged_decode_static(null, 0, 0, null, 0, 0, null, null, null, 0, null, 1, 14, 0, 1, 8, 2, 16, 64,
                                        _native.PSB_BF16, 16, 0.125, null, null) == _native.PSB_ERR_INVALID
-    # 256 sequences of up to 8192 tokens need ~115 MiB of split-K scratch
-    assert lib.psb_paged_decode_workspace_size(256, 14, 2, 64, 16, 8192, _native.PSB_BF16) > cap
+    # on the CUDA-core path (fp32 here), 256 sequences of up to 8192 tokens
+    # need ~115 MiB of per-chunk partials: rejected before any CUDA call
+    assert lib.psb_paged_decode_workspace_size(256, 14, 2, 64, 16, 8192, _native.PSB_F32) > cap
     assert lib.psb_paged_decode_static(fake, 896, 64, fake, 896, 64, fake, fake, fake, 512, fake, 256, 14, 0, 1,
+                                       40000, 2, 16, 64, _native.PSB_F32, 8192, 0.125, null,
+                                       null) == _native.PSB_ERR_WORKSPACE
+    # a misaligned bf16 query also takes that path, and is rejected the same way
+    assert lib.psb_paged_decode_static(fake + 2, 896, 64, fake, 896, 64, fake, fake, fake, 512, fake, 256, 14, 0, 1,
                                        40000, 2, 16, 64, _native.PSB_BF16, 8192, 0.125, null,
                                        null) == _native.PSB_ERR_WORKSPACE
     # 64 sequences of up to 4096 tokens fit

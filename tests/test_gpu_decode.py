@@ -161,7 +161,7 @@ def test_serving_scale_batch_256():
     rng = np.random.default_rng(2)
     lens = np.clip(np.round(rng.lognormal(math.log(1024), 0.8, 256)), 16, 8192).astype(int).tolist()
     c = _synthetic(3, lens)
-    out = _run_tensor_api(c, poison=False)
+    out = _run_tensor_api(c, poison=True)
     exact = ora.decode_attention(c["q"], c["k_cache"], c["v_cache"], c["tables"], c["context_lens"], c["layer"])
     mx, mean = err_stats(out, exact)
     assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)

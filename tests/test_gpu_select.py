@@ -139,10 +139,15 @@ def test_reference_facing_step():
     assert ids == tokens.view(-1).tolist()
     assert done == [False, True, True, False, False, False]
     assert rem.tolist() == [4, 0, 3, 1, 7, 1]
-    rem[0] = 0
+    rem.copy_(torch.tensor([4, 2, 3, 0, 7, 1], dtype=torch.int32))
+    before = rem.tolist()
     tokens, status = select_next_tokens(logits, eos, rem)
-    with pytest.raises(RuntimeError, match="generation limit"):
+    with pytest.raises(RuntimeError, match="generation limit") as info:
         read_selection(tokens, status)
+    # the rows before the failing one keep their tokens, as in the reference's loop
+    assert info.value.row == 3
+    assert info.value.tokens == tokens.view(-1).tolist()
+    assert rem.tolist() == [b - (0 if i == 3 else 1) for i, b in enumerate(before)]
 
 
 def test_graph_capture_replays():
@@ -171,3 +176,76 @@ def test_graph_capture_replays():
         assert rem.tolist() == [2 - step] * b
         assert bool((status == sel.DONE).all()) == (step == 2)
     graph.reset()
+
+
+def _stream_geometry(vocab: int, cluster: int, esz: int):
+    """The streaming kernel's split of a row, restated: CTA r of a cluster
+    owns elements [r * chunk, (r + 1) * chunk); inside it, warp w owns 16-byte
+    vectors [w0, w1) of an equal split over 8 warps; a warp streams them in
+    4 KB pieces of 256 vectors, lane l holding vectors l, l + 32, ... of a
+    piece.  Yields (slice start, slice vectors, per-warp (w0, w1))."""
+    n = 16 // esz
+    chunk = -(-(-(-vocab // cluster)) // n) * n
+    for r in range(cluster):
+        lo = r * chunk
+        cnt = max(0, min(vocab, lo + chunk) - lo)
+        nvec = cnt // n
+        per = -(-nvec // 8)
+        warps = [(min(nvec, w * per), min(nvec, min(nvec, w * per) + per)) for w in range(8)]
+        yield lo, cnt, warps
+
+
+def _planted_rows(vocab: int, cluster: int, esz: int):
+    """Pairs of equal maxima planted where the index search changes hands:
+    lane 31's last element of a warp's first piece against lane 0's first
+    element of its second piece (the later lane wins the piece order, the
+    earlier index wins the tie), a warp's last vector against the next
+    warp's first, either side of a CTA slice boundary, and the ragged tail
+    past the last whole vector."""
+    n = 16 // esz
+    pairs = []
+    for lo, cnt, warps in _stream_geometry(vocab, cluster, esz):
+        for w, (w0, w1) in enumerate(warps):
+            if w1 - w0 > 256:  # the warp has a second piece
+                a = lo + (w0 + 255) * n + n - 1   # lane 31, vector 7 of piece 0, last element
+                b = lo + (w0 + 256) * n           # lane 0, vector 0 of piece 1, first element
+                pairs.append((a, b))
+                pairs.append((lo + (w0 + 255) * n, b))
+                pairs.append((lo + (w0 + 31) * n + 3, lo + (w0 + 256 + 1) * n))  # lane 31 piece 0 vs lane 1 piece 1
+            if w + 1 < 8 and warps[w + 1][1] > warps[w + 1][0] and w1 > w0:
+                pairs.append((lo + w1 * n - 1, lo + w1 * n))
+        if lo > 0 and cnt > 0:
+            pairs.append((lo - 1, lo))
+        tail = lo + (cnt // n) * n
+        if tail < lo + cnt:  # elements past the slice's last whole vector
+            pairs.append((tail - 1, lo + cnt - 1))
+            pairs.append((lo + cnt - 1, lo + cnt - 1))
+    pairs.append((vocab - 2, vocab - 1))
+    return [p for p in pairs if 0 <= p[0] <= p[1] < vocab]
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+@pytest.mark.parametrize("vocab", [VOCAB, 70001])
+@pytest.mark.parametrize("ctas", [1, 2, 8])
+def test_first_maximum_at_stream_boundaries(dtype, vocab, ctas):
+    """Row maxima tied across the pieces, warps and CTAs of the streaming
+    kernel's schedule: the first index must win, as torch.argmax picks it."""
+    from pagedserve_b200 import ops
+    esz = 4 if dtype == "float32" else 2
+    pairs = _planted_rows(vocab, ctas, esz)
+    assert len(pairs) >= 4
+    g = torch.Generator(device="cuda").manual_seed(vocab + ctas)
+    # rows padded to a 16-byte pitch, so a ragged vocabulary still takes the
+    # streaming kernel (its rows start on 16-byte boundaries)
+    pitch = -(-vocab // 8) * 8
+    x = torch.rand(len(pairs), pitch, generator=g, device="cuda").to(TORCH_DTYPES[dtype])[:, :vocab]
+    for row, (a, b) in enumerate(pairs):
+        x[row, a] = 8.0
+        x[row, b] = 8.0
+    eos = torch.tensor([vocab + 1], dtype=torch.int64, device="cuda")
+    rem = torch.full((len(pairs),), 5, dtype=torch.int32, device="cuda")
+    tokens, _, _, err = _run(x, eos, rem, ctas)
+    assert err == 0
+    want = np.array([a for a, _ in pairs])
+    assert np.array_equal(tokens, want)
+    assert np.array_equal(tokens, x.argmax(dim=-1).cpu().numpy())

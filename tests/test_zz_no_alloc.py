@@ -25,9 +25,9 @@ def _cuda():
         pytest.fail("CUDA device required for -m gpu tests")
 
 
-def _case(dtype, batch, max_len, hq, hkv, d, bs, seed):
+def _case(dtype, batch, max_len, hq, hkv, d, bs, seed, typical=None):
     rng = np.random.default_rng(seed)
-    lens = [int(x) for x in rng.integers(1, max_len + 1, size=batch)]
+    lens = [int(x) for x in rng.integers(1, (typical or max_len) + 1, size=batch)]
     lens[0] = max_len
     need = [-(-n // bs) for n in lens]
     nb = sum(need) + 5
@@ -112,11 +112,43 @@ def test_static_decode_shrinking_then_growing_batch():
     assert int(err.item()) == 0
 
 
+def test_static_decode_serving_batch_fits():
+    """The serving batch (256 bf16 sequences, contexts up to 8192 tokens)
+    takes the fast path, whose scratch is a fixed ~10.8 MB: it fits the
+    array, matches the workspace entry point and the oracle."""
+    from pagedserve_b200 import _native, ops
+    lib = _native.load()
+    c = _case("bfloat16", 256, 8192, 14, 2, 64, 16, seed=8192, typical=1024)
+    q = to_dev(c["q"], "bfloat16")
+    k, v = to_dev(c["k"], "bfloat16"), to_dev(c["v"], "bfloat16")
+    table = torch.from_numpy(ora.padded_block_table(c["tables"])).cuda()
+    lens = torch.tensor(c["lens"], dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    want = ops.paged_decode(q, k, v, table, lens, c["layer"], max_context=c["max_context"])
+    outs = []
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        _native.check(_call_static(lib, q, out, k, v, table, lens, c["layer"], c["max_context"], err),
+                      "paged_decode_static")
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    rows = [0, 1, 77, 255]  # the oracle on a few rows (one with the longest context)
+    exact = ora.decode_attention(c["q"][rows], c["k"], c["v"], [c["tables"][r] for r in rows],
+                                 [c["lens"][r] for r in rows], c["layer"])
+    for out in outs:
+        torch.testing.assert_close(out.float(), want.float(), rtol=0, atol=2e-2)
+        mx, mean = err_stats(out[rows], exact)
+        assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
+
+
 def test_static_decode_rejects_oversized_geometry():
+    """The CUDA-core path (fp32) needs per-chunk partials that grow with
+    batch x context: 256 sequences of 8192 tokens exceed the array."""
     from pagedserve_b200 import _native
     lib = _native.load()
-    q = torch.zeros(256, 14, 64, dtype=torch.bfloat16, device="cuda")
-    k = torch.zeros(1, 8, 2, 16, 64, dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros(256, 14, 64, dtype=torch.float32, device="cuda")
+    k = torch.zeros(1, 8, 2, 16, 64, dtype=torch.float32, device="cuda")
     table = torch.zeros(256, 512, dtype=torch.int32, device="cuda")
     lens = torch.ones(256, dtype=torch.int32, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
