@@ -60,8 +60,10 @@ def test_decode_step_matches_reference_fp32():
     got, want, (kc, vc), (kc_ref, vc_ref) = _decode_case(torch.float32)
     diff = (got - want).abs()
     assert diff.max().item() <= 2e-4, diff.max().item()
-    torch.testing.assert_close(kc, kc_ref, rtol=0, atol=1e-6)
-    torch.testing.assert_close(vc, vc_ref, rtol=0, atol=1e-6)
+    # the new rows differ only by the projection GEMMs' fp32 summation order
+    # (one fused q|k|v GEMM here, three in transformers); RoPE itself is exact
+    torch.testing.assert_close(kc, kc_ref, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(vc, vc_ref, rtol=1e-5, atol=1e-5)
 
 
 def test_decode_step_bf16_tracks_reference():
