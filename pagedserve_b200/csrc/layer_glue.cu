@@ -100,6 +100,73 @@ __global__ void __launch_bounds__(kGlueThreads) add_rms_norm_kernel(
   }
 }
 
+// One CTA of kRowThreads per row, each thread holding up to MAXV vectors of
+// the row in registers: every load (x, residual, weight) is issued before
+// the first use, and one block-wide sum replaces the warp's serial passes.
+constexpr int kRowThreads = 128;
+
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(kRowThreads) add_rms_norm_row_kernel(
+    const T* __restrict__ x, int64_t xs, T* residual, int64_t rs, const T* __restrict__ weight, T* __restrict__ out,
+    int64_t os, int32_t hidden, float eps) {
+  __shared__ float s_part[kRowThreads / 32];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = hidden / VEC;
+  const T* xr = x + static_cast<int64_t>(row) * xs;
+  T* rr = residual != nullptr ? residual + static_cast<int64_t>(row) * rs : nullptr;
+  Pack<T, VEC> a[MAXV], w[MAXV];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * kRowThreads;
+    if (i < nvec) {
+      a[k] = load_pack<T, VEC>(xr + i * VEC);
+      w[k] = load_pack<T, VEC>(weight + i * VEC);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * kRowThreads;
+    if (i < nvec) {
+      if (rr != nullptr) {
+        const Pack<T, VEC> b = *reinterpret_cast<const Pack<T, VEC>*>(rr + i * VEC);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          a[k].v[j] = Elem<T>::from_float(Elem<T>::to_float(a[k].v[j]) + Elem<T>::to_float(b.v[j]));
+        store_pack<T, VEC>(rr + i * VEC, a[k]);
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = Elem<T>::to_float(a[k].v[j]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if ((tid & 31) == 0) s_part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; ++i) tot += s_part[i];
+  const float inv = rsqrtf(tot / static_cast<float>(hidden) + eps);
+  T* dst = out + static_cast<int64_t>(row) * os;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int i = tid + k * kRowThreads;
+    if (i < nvec) {
+      Pack<T, VEC> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const T n = Elem<T>::from_float(Elem<T>::to_float(a[k].v[j]) * inv);
+        o.v[j] = Elem<T>::from_float(Elem<T>::to_float(w[k].v[j]) * Elem<T>::to_float(n));
+      }
+      store_pack<T, VEC>(dst + i * VEC, o);
+    }
+  }
+}
+
 // out[r, j] = round(round(silu(g)) * u), g = gate_up[r, j], u = gate_up[r, inter + j].
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kGlueThreads) silu_and_mul_kernel(const T* __restrict__ gu, int64_t gs,
@@ -133,8 +200,28 @@ int launch_add_rms_norm(const void* x, int64_t xs, void* residual, int64_t rs, c
   constexpr int VEC = 16 / sizeof(T);
   const bool vec = hidden % VEC == 0 && xs % VEC == 0 && os % VEC == 0 && aligned16(x) && aligned16(weight) &&
                    aligned16(out) && (residual == nullptr || (rs % VEC == 0 && aligned16(residual)));
-  const unsigned grid = static_cast<unsigned>((static_cast<int64_t>(rows) * 32 + kGlueThreads - 1) / kGlueThreads);
   discard_stale_error();
+  if (vec) {
+    // one CTA per row while the row fits the CTA's registers (hidden up to
+    // 4096 bf16 / 2048 fp32 elements)
+    const int per = (hidden / VEC + kRowThreads - 1) / kRowThreads;
+    const T* xt = static_cast<const T*>(x);
+    T* rt = static_cast<T*>(residual);
+    const T* wt = static_cast<const T*>(weight);
+    T* ot = static_cast<T*>(out);
+    const unsigned g = static_cast<unsigned>(rows);
+    switch (per) {
+      case 1: add_rms_norm_row_kernel<T, VEC, 1><<<g, kRowThreads, 0, s>>>(xt, xs, rt, rs, wt, ot, os, hidden, eps);
+        return check_launch();
+      case 2: add_rms_norm_row_kernel<T, VEC, 2><<<g, kRowThreads, 0, s>>>(xt, xs, rt, rs, wt, ot, os, hidden, eps);
+        return check_launch();
+      case 3:
+      case 4: add_rms_norm_row_kernel<T, VEC, 4><<<g, kRowThreads, 0, s>>>(xt, xs, rt, rs, wt, ot, os, hidden, eps);
+        return check_launch();
+      default: break;
+    }
+  }
+  const unsigned grid = static_cast<unsigned>((static_cast<int64_t>(rows) * 32 + kGlueThreads - 1) / kGlueThreads);
   if (vec)
     add_rms_norm_kernel<T, VEC><<<grid, kGlueThreads, 0, s>>>(
         static_cast<const T*>(x), xs, static_cast<T*>(residual), rs, static_cast<const T*>(weight),
