@@ -76,6 +76,19 @@ def _memo(cache, kind: str, request_ids, positions, device, build):
     return value
 
 
+def _last_hit(cache, kind: str, request_ids, positions, device):
+    """The metadata the last call of this kind built for the same epoch,
+    request list and positions, or None (two list comparisons)."""
+    last = getattr(cache, "_psb_last", None)
+    if last is None or type(request_ids) is not list or type(positions) is not list:
+        return None
+    hit = last.get(kind)
+    if (hit is not None and hit[0] == getattr(cache, "metadata_epoch", None) and hit[1] == str(device)
+            and hit[2] == request_ids and hit[3] == positions):
+        return hit[4]
+    return None
+
+
 def clear_metadata_cache(cache) -> None:
     """Drop the device copies of block tables and slots kept on ``cache``."""
     store = getattr(cache, "_psb_metadata", None)
@@ -96,19 +109,24 @@ def _host_metadata(cache, request_ids, positions, device):
 
 
 def _build_metadata(cache, request_ids, positions, device):
-    if hasattr(cache, "token_counts") and hasattr(cache, "table_rows"):
-        # this package's PagedKVCache: vectorised over its table store
-        counts = cache.token_counts(request_ids)
+    if hasattr(cache, "gather_tables"):
+        # this package's PagedKVCache: vectorised over its table store, the
+        # table gathered straight into pinned memory as [table (B x W) | lengths (B)]
+        rows = cache.table_store_rows(request_ids)
+        counts = cache.store_token_counts(rows)
         pos = np.asarray(positions, dtype=np.int64)
         bad = np.flatnonzero((pos < 0) | (pos >= counts))
         if bad.size:
             row = int(bad[0])
             raise ValueError(f"Invalid position {positions[row]} for {request_ids[row]}")
-        table = cache.table_rows(request_ids)
-        width = table.shape[1]
-        packed = np.empty((len(request_ids), width + 1), dtype=np.int32)  # [table | length]
-        packed[:, :width] = table
-        packed[:, width] = pos + 1
+        b = len(request_ids)
+        width = cache.table_width(rows)
+        host = torch.empty(b * (width + 1), dtype=torch.int32, pin_memory=device.type == "cuda")
+        flat = host.numpy()
+        cache.gather_tables(rows, flat, width)
+        flat[b * width:] = pos + 1
+        dev = host.to(device, non_blocking=True)
+        return _Meta(dev[: b * width].view(b, width), dev[b * width:], width)
     else:
         # any cache with the reference's interface
         lengths = np.empty(len(request_ids), dtype=np.int32)
@@ -128,7 +146,25 @@ def _build_metadata(cache, request_ids, positions, device):
     if device.type == "cuda":
         host = host.pin_memory()
     dev = host.to(device, non_blocking=True)
-    return dev[:, :width], dev[:, width].contiguous(), width
+    return _Meta(dev[:, :width], dev[:, width].contiguous(), width)
+
+
+class _Meta:
+    """A decode batch's device table and lengths, and the launch arguments
+    that stay the same for all layer calls over them (``ops.DecodeLaunch``,
+    built on the first call)."""
+
+    __slots__ = ("tables", "lengths", "width", "launch")
+
+    def __init__(self, tables, lengths, width):
+        self.tables, self.lengths, self.width = tables, lengths, width
+        self.launch = None
+
+    def __iter__(self):  # (tables, lengths, width)
+        return iter((self.tables, self.lengths, self.width))
+
+    def __getitem__(self, i):
+        return (self.tables, self.lengths, self.width)[i]
 
 
 def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str], positions: Sequence[int],
@@ -137,9 +173,18 @@ def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str
 
     Drop-in for ``triton_paged_decode_attention`` (triton_paged_decode.py:98-104).
     """
-    tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
+    meta = _validated_metadata(query, cache, request_ids, positions, layer)
+    return _launch(meta, cache, query, layer)
+
+
+def _launch(meta: "_Meta", cache, query, layer, new_key=None, new_value=None):
     kv = cache.kv_cache
-    return ops._decode_checked(query, kv.k_cache, kv.v_cache, tables, lengths, layer, width * cache.block_size)
+    launch = meta.launch
+    if launch is None or not launch.matches(kv.k_cache, kv.v_cache, query):
+        launch = meta.launch = ops.DecodeLaunch(kv.k_cache, kv.v_cache, meta.tables, meta.lengths,
+                                                query.shape[0], query.shape[1], meta.width * cache.block_size,
+                                                query.dtype)
+    return launch(query, layer, new_key, new_value)
 
 
 def _validated_metadata(query, cache, request_ids, positions, layer):
@@ -160,7 +205,10 @@ def _validated_metadata(query, cache, request_ids, positions, layer):
         raise ValueError("Batch must not be empty")
     if len(request_ids) != batch or len(positions) != batch:
         raise ValueError("Request IDs and positions must match batch size")
-    if len(set(request_ids)) != batch:
+    # the metadata of an earlier call with these very lists was built only
+    # after they passed every check here, uniqueness included
+    meta = _last_hit(cache, "table", request_ids, positions, query.device)
+    if meta is None and len(set(request_ids)) != batch:
         raise ValueError("Request IDs must be unique")
     if head_dim != kv.head_dim:
         raise ValueError("Head dimension mismatch")
@@ -172,8 +220,9 @@ def _validated_metadata(query, cache, request_ids, positions, layer):
         raise ValueError("Query and cache must be on the same device")
     if not 0 <= layer < kv.k_cache.shape[0]:
         raise ValueError("Invalid layer")
-    tables, lengths, width = _host_metadata(cache, request_ids, positions, query.device)
-    return tables, lengths, width
+    if meta is None:
+        meta = _host_metadata(cache, request_ids, positions, query.device)
+    return meta
 
 
 def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, cache,
@@ -192,18 +241,29 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     if not query.is_cuda:
         raise ValueError(_CUDA_REQUIRED)
     kv = cache.kv_cache
-    if key.ndim == 4:
-        key, value = key.squeeze(2), value.squeeze(2)
     shape = (kv.num_kv_heads, kv.head_dim)
-    if tuple(key.shape[1:]) != shape or tuple(value.shape[1:]) != shape:
+    # [B, Hkv, 1, D] as the glue holds them, or [B, Hkv, D]; the launch reads
+    # the batch and head strides, which are the same either way
+    if _rows_shape(key) != shape or _rows_shape(value) != shape:
         raise ValueError(f"Expected K/V shape {shape}; got key={tuple(key.shape)}, value={tuple(value.shape)}")
     if key.dtype != kv.dtype or value.dtype != kv.dtype:
         raise ValueError(f"K/V tensors must have dtype {kv.dtype}")
     if key.shape[0] != query.shape[0] or value.shape[0] != query.shape[0]:
         raise ValueError("Request IDs and positions must match batch size")
-    tables, lengths, width = _validated_metadata(query, cache, request_ids, positions, layer)
-    return ops._decode_checked(query, kv.k_cache, kv.v_cache, tables, lengths, layer, width * cache.block_size,
-                               new_key=key, new_value=value)
+    meta = _validated_metadata(query, cache, request_ids, positions, layer)
+    if key.device != query.device or value.device != query.device:
+        raise ValueError("new K/V must be on the query's device")
+    return _launch(meta, cache, query, layer, key, value)
+
+
+def _rows_shape(t: torch.Tensor) -> tuple:
+    """(heads, head_dim) of new rows given as [B, H, D] or [B, H, 1, D] (else a shape that matches nothing)."""
+    shp = t.shape
+    if len(shp) == 3:
+        return (shp[1], shp[2])
+    if len(shp) == 4 and shp[2] == 1:
+        return (shp[1], shp[3])
+    return tuple(shp)
 
 
 def write_tokens(cache, request_ids: Sequence[str], positions: Sequence[int], layer: int, key: torch.Tensor,

@@ -26,6 +26,9 @@ struct PrefillParams {
   const int32_t* ctx = nullptr;
   int32_t layer = 0, num_layers_total = 0, block_size = 0, max_context = 0;
   int64_t num_blocks = 0;
+  // tcgen05 kernel: room in shared memory for this many tiles per CTA (set
+  // by the launch from an upper bound of the tiles and the grid)
+  int32_t max_cta_tiles = 0;
 };
 
 // tcgen05 / TMEM kernel (varlen_prefill_tc.cu): bf16/f16, head_dim 64,

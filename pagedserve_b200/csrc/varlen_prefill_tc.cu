@@ -136,6 +136,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   int32_t* s_cnt = s_lstart + (max_level + 1);   // [max_level + 1] sequences with more than i blocks
   int32_t* s_fill = s_cnt + (max_level + 1);     // [max_level + 1] placement cursors
   int32_t* s_sorted = s_fill + (max_level + 1);  // [num_seqs] sequences by query blocks, descending, stable
+  // [max_cta_tiles][2] this CTA's tiles: {seq, qblk, head, q0}, {len, ctx, n_kv, 0}
+  int4* s_tiles = reinterpret_cast<int4*>(
+      (reinterpret_cast<uintptr_t>(s_sorted + p.num_seqs) + 15) & ~uintptr_t(15));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hq = p.hq, group = p.hq / p.hkv;
@@ -187,8 +190,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int rounds = total_tiles / G, rem = total_tiles - rounds * G;
   const int my_tiles = rounds + (((rounds & 1) ? G - 1 - c : c) < rem ? 1 : 0);
   if (my_tiles == 0) return;
-  // k-th tile of this CTA
-  auto tile_of = [&](int k) -> TileInfo {
+  if (my_tiles > p.max_cta_tiles) {  // the launch sized the tile list too small: nothing is computed
+    if (tid == 0) flag_error(p.err, PSB_DEVERR_WORKSPACE);
+    return;
+  }
+  // k-th tile of this CTA, from the sorted sequences and cu_seqlens
+  auto compute_tile = [&](int k) -> TileInfo {
     const int t = k * G + ((k & 1) ? G - 1 - c : c);
     const int tt = t / hq;
     int lo = 0, hi = max_level - 1;  // the smallest level i with lstart_i <= T
@@ -215,6 +222,29 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
     ti.start = ti.ctx - ti.len;
     ti.n_kv = (ti.start + min(ti.len, (lo + 1) * kBM) + kBN - 1) / kBN;  // keys [0, start + last row + 1)
+    return ti;
+  };
+  // Every tile of this CTA is worked out once, here, by all threads at once:
+  // a tile's cu_seqlens (and context) loads would otherwise sit on each
+  // role's critical path at every tile change.
+  for (int k = tid; k < my_tiles; k += kTcThreads) {
+    const TileInfo ti = compute_tile(k);
+    s_tiles[2 * k] = make_int4(ti.seq, ti.qblk, ti.head, ti.q0);
+    s_tiles[2 * k + 1] = make_int4(ti.len, ti.ctx, ti.n_kv, 0);
+  }
+  __syncthreads();
+  auto tile_of = [&](int k) -> TileInfo {
+    const int4 a = s_tiles[2 * k], b = s_tiles[2 * k + 1];
+    TileInfo ti;
+    ti.seq = a.x;
+    ti.qblk = a.y;
+    ti.head = a.z;
+    ti.q0 = a.w;
+    ti.kvh = ti.head / group;
+    ti.len = b.x;
+    ti.ctx = b.y;
+    ti.n_kv = b.z;
+    ti.start = ti.ctx - ti.len;
     return ti;
   };
   const uint32_t s_base = smem_u32(smem);
@@ -598,8 +628,19 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   }
 }
 
-size_t tc_smem_bytes(int max_level, int num_seqs) {
-  return 1024 + kSmemTiles + kSmemBars + sizeof(int32_t) * (3 * (static_cast<size_t>(max_level) + 1) + num_seqs);
+size_t tc_smem_bytes(int max_level, int num_seqs, int max_cta_tiles) {
+  return 1024 + kSmemTiles + kSmemBars + sizeof(int32_t) * (3 * (static_cast<size_t>(max_level) + 1) + num_seqs) +
+         16 + 2 * sizeof(int4) * static_cast<size_t>(max_cta_tiles);
+}
+
+// An upper bound of the tiles: sum over sequences of ceil(len / 128), times the heads.
+int64_t tc_tiles_bound(const PrefillParams& p) { return (static_cast<int64_t>(p.total) / kBM + p.num_seqs) * p.hq; }
+
+// Tiles per CTA that any persistent grid of at least one CTA per SM (or one
+// CTA per tile, when there are fewer tiles) can deal to one CTA.
+int tc_max_cta_tiles(const PrefillParams& p, int sms) {
+  const int64_t tiles = tc_tiles_bound(p);
+  return static_cast<int>(std::min<int64_t>(tiles, (tiles + sms - 1) / std::max(sms, 1) + 1));
 }
 
 }  // namespace
@@ -614,11 +655,15 @@ bool prefill_tc_supported(const PrefillParams& p, int dtype) {
   const bool strides = p.qst % 8 == 0 && p.qsh % 8 == 0 && kv_strides && p.ost % 2 == 0 && p.osh % 2 == 0 &&
                        p.qst > 0;
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
+  const int sms = device_sm_count();
+  if (sms <= 0) return false;
   return strides && al16(p.q) && al16(p.k) && al16(p.v) && reinterpret_cast<uintptr_t>(p.out) % 4 == 0 &&
-         max_level <= kMaxLevels && p.num_seqs <= kMaxTcSeqs && tc_smem_bytes(max_level, p.num_seqs) <= 227 * 1024;
+         max_level <= kMaxLevels && p.num_seqs <= kMaxTcSeqs &&
+         tc_smem_bytes(max_level, p.num_seqs, tc_max_cta_tiles(p, sms)) <= 227 * 1024;
 }
 
-int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
+int prefill_tc_launch(const PrefillParams& p_in, int dtype, cudaStream_t s) {
+  PrefillParams p = p_in;
   const CUtensorMapDataType dt = dtype == PSB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tq, tk, tv;
   if (!encode_rows_map(&tq, p.q, p.total, p.hq, kDim, p.qst, p.qsh, kBM, dt)) return PSB_ERR_CUDA;
@@ -632,18 +677,18 @@ int prefill_tc_launch(const PrefillParams& p, int dtype, cudaStream_t s) {
     return PSB_ERR_CUDA;
   }
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
-  // an upper bound of the tiles: sum over sequences of ceil(len / 128), times the heads
-  const int64_t tiles = (static_cast<int64_t>(p.total) / kBM + p.num_seqs) * p.hq;
+  const int64_t tiles = tc_tiles_bound(p);
   if (tiles == 0) return PSB_OK;
   if (tiles >= (int64_t(1) << 31)) return PSB_ERR_UNSUPPORTED;
-  const size_t smem = tc_smem_bytes(max_level, p.num_seqs);
+  const int sms = device_sm_count();
+  if (sms <= 0) return PSB_ERR_CUDA;
+  p.max_cta_tiles = tc_max_cta_tiles(p, sms);
+  const size_t smem = tc_smem_bytes(max_level, p.num_seqs, p.max_cta_tiles);
   const auto bf = p.paged ? prefill_tc_kernel<__nv_bfloat16, true> : prefill_tc_kernel<__nv_bfloat16, false>;
   const auto hf = p.paged ? prefill_tc_kernel<__half, true> : prefill_tc_kernel<__half, false>;
   const void* kern = dtype == PSB_BF16 ? reinterpret_cast<const void*>(bf) : reinterpret_cast<const void*>(hf);
   int occ = 0;
   if (!kernel_occupancy(kern, kTcThreads, smem, &occ) || occ < 1) return PSB_ERR_CUDA;
-  const int sms = device_sm_count();
-  if (sms <= 0) return PSB_ERR_CUDA;
   const int64_t grid = std::min<int64_t>(tiles, static_cast<int64_t>(sms) * occ);  // persistent
   discard_stale_error();
   cudaError_t e;

@@ -272,50 +272,63 @@ def paged_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
-def _decode_checked(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, tables: torch.Tensor,
-                    lengths: torch.Tensor, layer: int, max_context: int, new_key: torch.Tensor | None = None,
-                    new_value: torch.Tensor | None = None) -> torch.Tensor:
-    """paged_decode for the reference-facing wrappers, whose arguments are
-    already checked: ``query [B, Hq, 1, D]`` on the pools' device with their
-    dtype, contiguous pools, device tables ``[B, M]`` int32 with unit inner
-    stride and contiguous int32 lengths from the metadata builder, and new
-    rows of shape ``[B, Hkv(, 1), D]`` and the pools' dtype.  Only what the
-    launch itself needs is looked at (the public ``paged_decode`` repeats
-    every check; this path runs once per layer per decode iteration)."""
-    nl, nb, hkv, bs, d = k_cache.shape
-    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
-        raise ValueError("KV pools must be contiguous")
-    if query.stride(3) != 1:
-        query = query.contiguous()
-    bsz, hq = query.shape[0], query.shape[1]
-    out = torch.empty_like(query)
-    need = decode_workspace_bytes(bsz, hq, hkv, d, bs, max_context, query.dtype)
-    ws = DecodeWorkspace.for_device(query.device).get(need, bsz, hkv)
-    lib = _native.load()
-    dt = _DTYPES[query.dtype]
-    stream = _stream(query.device)
-    scale = 1.0 / math.sqrt(d)
-    if new_key is None:
-        _native.check(lib.psb_paged_decode(
-            query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
-            k_cache.data_ptr(), v_cache.data_ptr(), tables.data_ptr(), tables.stride(0), lengths.data_ptr(), bsz, hq,
-            layer, nl, nb, hkv, bs, d, dt, max_context, scale, ws.data_ptr(), ws.numel(), None, stream),
-            "paged_decode")
+class DecodeLaunch:
+    """The launch arguments of one decode batch that stay the same for all
+    the layer calls of an iteration (pools, device table and lengths,
+    geometry, workspace), kept by the reference-facing wrappers next to the
+    batch's metadata so a repeat layer call only adds the query, output, new
+    rows, layer and stream before one C call.
+
+    Built from arguments the wrappers have already checked: pools contiguous
+    and of the query's dtype, device table ``[B, M]`` int32 with unit inner
+    stride and contiguous int32 lengths.  The workspace it sized is held
+    here, so a later growth of the per-device workspace never leaves this
+    launch pointing at freed memory."""
+
+    __slots__ = ("lib", "k_ptr", "v_ptr", "batch", "q_heads", "dtype", "dev", "ws", "table_args", "tail")
+
+    def __init__(self, k_cache: torch.Tensor, v_cache: torch.Tensor, tables: torch.Tensor, lengths: torch.Tensor,
+                 batch: int, q_heads: int, max_context: int, dtype: torch.dtype):
+        nl, nb, hkv, bs, d = (int(x) for x in k_cache.shape)
+        if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+            raise ValueError("KV pools must be contiguous")
+        self.lib = _native.load()
+        self.k_ptr, self.v_ptr = k_cache.data_ptr(), v_cache.data_ptr()
+        self.batch, self.q_heads, self.dtype = int(batch), int(q_heads), dtype
+        self.dev = k_cache.device.index if k_cache.device.index is not None else torch.cuda.current_device()
+        need = decode_workspace_bytes(self.batch, self.q_heads, hkv, d, bs, int(max_context), dtype)
+        self.ws = DecodeWorkspace.for_device(k_cache.device).get(need, self.batch, hkv)
+        self.table_args = (tables.data_ptr(), tables.stride(0), lengths.data_ptr(), self.batch, self.q_heads)
+        self.tail = (nl, nb, hkv, bs, d, _DTYPES[dtype], int(max_context), 1.0 / math.sqrt(d), self.ws.data_ptr(),
+                     self.ws.numel() * self.ws.element_size(), None)
+
+    def matches(self, k_cache: torch.Tensor, v_cache: torch.Tensor, query: torch.Tensor) -> bool:
+        return (k_cache.data_ptr() == self.k_ptr and v_cache.data_ptr() == self.v_ptr
+                and query.shape[0] == self.batch and query.shape[1] == self.q_heads and query.dtype == self.dtype)
+
+    def __call__(self, query: torch.Tensor, layer: int, new_key: torch.Tensor | None = None,
+                 new_value: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode (with ``new_key``/``new_value``: the fused write + decode)
+        for ``query [B, Hq, (1,) D]``; returns a new output of its shape."""
+        if query.stride(-1) != 1:
+            query = query.contiguous()
+        out = torch.empty_like(query)
+        stream = _raw_stream(self.dev) if _raw_stream is not None else torch.cuda.current_stream(self.dev).cuda_stream
+        head = (query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+                self.k_ptr, self.v_ptr)
+        if new_key is None:
+            _native.check(self.lib.psb_paged_decode(*head, *self.table_args, layer, *self.tail, stream),
+                          "paged_decode")
+            return out
+        if new_key.stride(-1) != 1:
+            new_key = new_key.contiguous()
+        if new_value.stride(-1) != 1:
+            new_value = new_value.contiguous()
+        _native.check(self.lib.psb_paged_decode_append(
+            *head, new_key.data_ptr(), new_key.stride(0), new_key.stride(1), new_value.data_ptr(),
+            new_value.stride(0), new_value.stride(1), *self.table_args, layer, *self.tail, stream),
+            "paged_decode_append")
         return out
-    if new_key.device != query.device or new_value.device != query.device:
-        raise ValueError("new K/V must be on the query's device")
-    nk = new_key.squeeze(2) if new_key.ndim == 4 else new_key
-    nv = new_value.squeeze(2) if new_value.ndim == 4 else new_value
-    if nk.stride(2) != 1:
-        nk = nk.contiguous()
-    if nv.stride(2) != 1:
-        nv = nv.contiguous()
-    _native.check(lib.psb_paged_decode_append(
-        query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
-        k_cache.data_ptr(), v_cache.data_ptr(), nk.data_ptr(), nk.stride(0), nk.stride(1), nv.data_ptr(), nv.stride(0),
-        nv.stride(1), tables.data_ptr(), tables.stride(0), lengths.data_ptr(), bsz, hq, layer, nl, nb, hkv, bs, d, dt,
-        max_context, scale, ws.data_ptr(), ws.numel(), None, stream), "paged_decode_append")
-    return out
 
 
 def varlen_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,

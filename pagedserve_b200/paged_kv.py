@@ -372,6 +372,30 @@ class PagedKVCache:
         out[:, :have] = self._store[rows, :have]
         return out
 
+    def table_store_rows(self, request_ids) -> np.ndarray:
+        """int64 ``[B]`` rows of ``request_ids`` in the table store (for
+        ``gather_tables``; raises KeyError for an unknown request)."""
+        return self._rows_of(request_ids)
+
+    def table_width(self, rows: np.ndarray) -> int:
+        """Blocks in the longest table of store ``rows`` (at least 1)."""
+        return max(int(self._store_blocks[rows].max()), 1) if len(rows) else 1
+
+    def gather_tables(self, rows: np.ndarray, out: np.ndarray, width: int) -> None:
+        """Write the block tables of store ``rows``, zero padded to ``width``
+        (>= ``table_width(rows)``), into the first ``len(rows) * width``
+        elements of ``out`` (int32, C-contiguous) as ``[B, width]``."""
+        dst = out[: len(rows) * width].reshape(len(rows), width)
+        have = min(width, self._store.shape[1])
+        np.take(self._store[:, :have], rows, axis=0, out=dst[:, :have] if have == width else None, mode="clip")
+        if have < width:
+            dst[:, :have] = self._store[rows, :have]
+            dst[:, have:] = 0
+
+    def store_token_counts(self, rows: np.ndarray) -> np.ndarray:
+        """int64 token counts of store ``rows``."""
+        return self._store_tokens[rows]
+
     def token_counts(self, request_ids) -> np.ndarray:
         """int64 ``[B]`` token counts of ``request_ids``."""
         return self._store_tokens[self._rows_of(request_ids)]
