@@ -872,10 +872,11 @@ def run_b200(args, world, rank, local):
 
     # ---- end to end through the reference-facing API, host buffers -------
     # Every step copies its inputs (q, new k, new v: one pinned staging
-    # buffer) to the device and its output back to pinned host memory.  The
-    # uploads run on their own stream into two alternating device buffers
-    # and the downloads on a third, so step s + 1's upload and step s - 1's
-    # download overlap step s's kernel, as a serving loop pipelines them.
+    # buffer) to the device and its output back to pinned host memory.  One
+    # copy stream carries, per step s, the read-back of step s - 1's output
+    # and the upload of step s + 1's inputs (two alternating device input
+    # buffers), so both overlap step s's kernel, as a serving loop pipelines
+    # them; one event orders each direction.
     cache, ids, positions = w["cache"], w["ids"], w["positions"]
     q_bytes, kv_bytes = w["q"].numel() * 2, w["new_k"].numel() * 2
     in_host = torch.empty(q_bytes + 2 * kv_bytes, dtype=torch.uint8).pin_memory()
@@ -887,60 +888,76 @@ def run_b200(args, world, rank, local):
               buf[q_bytes:q_bytes + kv_bytes].view(torch.bfloat16).view(batch, HKV, D),
               buf[q_bytes + kv_bytes:].view(torch.bfloat16).view(batch, HKV, D)) for buf in in_dev]
     o_host = [torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    s_up, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    s_copy = torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
     o_keep = [None, None]
 
     from pagedserve_b200.attention import clear_metadata_cache
 
-    def e2e_step(s):
+    def upload(s):  # step s's inputs into buffer s % 2 (its last reader, step s - 2, is done)
+        in_dev[s % 2].copy_(in_host, non_blocking=True)
+        ev_in[s % 2].record(s_copy)
+
+    def read_back(s):  # step s's output, once its kernel is done
+        s_copy.wait_event(ev_done[s % 2])
+        o_host[s % 2].copy_(o_keep[s % 2], non_blocking=True)
+
+    # Each decode iteration passes new positions, as a serving loop does: here
+    # iteration k decodes at positions ctx - 1 - k (inside each request's
+    # reserved capacity), so its first layer call rebuilds and copies the
+    # lengths; the block table stays on the device while the cache epoch and
+    # the request list do not change.
+    iter_positions = [[p - k for p in positions] for k in range(4)]
+
+    def e2e_step(s, first_iteration):
         i, layer = s % 2, s % LAYERS
-        if layer == 0:  # a new decode iteration: block tables are rebuilt and copied once
-            clear_metadata_cache(cache)
-        torch.cuda.set_stream(s_up)
-        if s >= 2:
-            s_up.wait_event(ev_done[i])  # step s - 2's kernel has read this input buffer
-        in_dev[i].copy_(in_host, non_blocking=True)
-        ev_in[i].record(s_up)
+        pos = iter_positions[first_iteration + s // LAYERS]
+        torch.cuda.set_stream(s_copy)
+        if s >= 1:
+            read_back(s - 1)  # also orders the upload below after step s - 1's kernel
+        upload(s + 1)
         torch.cuda.set_stream(compute)
         compute.wait_event(ev_in[i])
-        if s >= 2:
-            # step s - 2's output has been read back: only now may its memory
-            # go to this step's output
-            compute.wait_event(ev_out[i])
+        # step s - 2's output: its read-back precedes ev_in[i] on the copy stream
         o_keep[i] = None
         qd, kd, vd = views[i]
-        o = paged_decode_attention_with_write(qd, kd, vd, cache, ids, positions, layer)
-        o_keep[i] = o
+        o_keep[i] = paged_decode_attention_with_write(qd, kd, vd, cache, ids, pos, layer)
         ev_done[i].record(compute)
-        torch.cuda.set_stream(s_down)
-        s_down.wait_event(ev_done[i])
-        o_host[i].copy_(o, non_blocking=True)
-        ev_out[i].record(s_down)
-        torch.cuda.set_stream(compute)
 
-    for s in range(min(args.warmup, 3) * 2):
-        e2e_step(s)
+    def e2e_run(n, first_iteration):
+        torch.cuda.set_stream(s_copy)
+        s_copy.wait_stream(compute)
+        upload(0)
+        torch.cuda.set_stream(compute)
+        for s in range(n):
+            e2e_step(s, first_iteration)
+        torch.cuda.set_stream(s_copy)
+        read_back(n - 1)
+        torch.cuda.set_stream(compute)
+        compute.wait_stream(s_copy)
+
+    # one whole decode iteration of warm-up (pinned staging and the metadata
+    # path warm), then whole iterations timed: every iteration's first layer
+    # call rebuilds and copies the block tables, as a new iteration would
+    e2e_steps = 2 * LAYERS
+    clear_metadata_cache(cache)
+    e2e_run(LAYERS, 0)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e_start.record(compute)
-    s_up.wait_stream(compute)
-    for s in range(args.steps):
-        e2e_step(s)
-    compute.wait_stream(s_down)
+    e2e_run(e2e_steps, 1)
     e_end.record(compute)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = e_start.elapsed_time(e_end) / args.steps
-    width = cache.table_rows(ids).shape[1]
-    iterations = -(-args.steps // LAYERS)  # metadata copies inside the timed region
-    meta_bytes = 4 * batch * (width + 1)  # table + lengths
-    h2d = in_host.numel() + meta_bytes * iterations / args.steps
+    e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
+    iterations = e2e_steps // LAYERS  # lengths copies inside the timed region
+    h2d = in_host.numel() + 4 * batch * iterations / e2e_steps
+    # iteration k attends over ctx - k tokens per request
+    e2e_rank_bytes = sum(decode_bytes(w["lens"] - k) + reshape_bytes(batch) for k in range(1, 1 + iterations)) / iterations
     d2h = o_host[0].numel() * 2
 
     # ---- reduce over ranks (gloo, host tensors): times by max, work by sum ----
@@ -949,8 +966,8 @@ def run_b200(args, world, rank, local):
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
     rank_step_ms = step_ms
     per_rank = gather_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
-                                "two_ms": two_ms, "bytes": step_bytes, "seqs": batch, "ctx": int(lens.sum())},
-                               host_group)
+                                "two_ms": two_ms, "bytes": step_bytes, "e2e_bytes": e2e_rank_bytes, "seqs": batch,
+                                "ctx": int(lens.sum())}, host_group)
     step_ms, dec_ms, e2e_ms, single_ms, two_ms = (max(r[k] for r in per_rank) for k in
                                                  ("step_ms", "dec_ms", "e2e_ms", "single_ms", "two_ms"))
     total_bytes, total_seqs = sum(r["bytes"] for r in per_rank), int(sum(r["seqs"] for r in per_rank))
@@ -964,7 +981,7 @@ def run_b200(args, world, rank, local):
     torch.cuda.empty_cache()
     serving = run_serving(args, device, world, rank, host_group) if "serve" in sections else None
     value = total_bytes / (step_ms * 1e-3) / 1e9
-    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    e2e_value = sum(r["e2e_bytes"] for r in per_rank) / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = load_peaks()
     achieved = step_bytes / (rank_step_ms * 1e-3) / 1e9
 
@@ -999,12 +1016,15 @@ def run_b200(args, world, rank, local):
                          "decode_only_ms": round(dec_ms, 5),
                          "decode_only_note": "decode + combine without the new-token store, same graphs"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
                     "path": "per layer call: q, new k, new v copied from one pinned host staging buffer, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
-                            "one launch), output copied back to pinned host memory; uploads and downloads on their "
-                            "own streams (two alternating device input buffers), so they overlap the neighbouring "
-                            f"steps' kernels; block tables built and copied once per {LAYERS}-layer iteration"},
+                            "one launch), output copied back to pinned host memory; the read-back of step s - 1 "
+                            "and the upload of step s + 1 (two alternating device input buffers) on one copy "
+                            "stream, overlapping step s's kernel; each iteration's first layer call rebuilds and "
+                            "copies the lengths for its new positions (the block table stays on the device within "
+                            f"a cache epoch); timed over 2 whole iterations ({LAYERS} layer calls each) after one "
+                            "of warm-up"},
             "gpu_launches": 2 * args.steps,
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
             "clocks": clocks.summary(),

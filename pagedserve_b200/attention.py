@@ -50,7 +50,7 @@ def _memo(cache, kind: str, request_ids, positions, device, build):
     epoch = getattr(cache, "metadata_epoch", None)
     if epoch is None:
         return build()
-    dev = str(device)
+    dev = device
     lists = type(request_ids) is list and type(positions) is list
     last = getattr(cache, "_psb_last", None)
     if last is None:
@@ -62,7 +62,8 @@ def _memo(cache, kind: str, request_ids, positions, device, build):
     store = getattr(cache, "_psb_metadata", None)
     if store is None:
         store = cache._psb_metadata = OrderedDict()
-    key = (kind, epoch, tuple(request_ids), tuple(int(p) for p in positions), dev)
+    # tuples built at C speed (numpy and Python integers hash alike)
+    key = (kind, epoch, tuple(request_ids), tuple(positions), dev)
     value = store.get(key)
     if value is not None:
         store.move_to_end(key)
@@ -83,20 +84,22 @@ def _last_hit(cache, kind: str, request_ids, positions, device):
     if last is None or type(request_ids) is not list or type(positions) is not list:
         return None
     hit = last.get(kind)
-    if (hit is not None and hit[0] == getattr(cache, "metadata_epoch", None) and hit[1] == str(device)
+    if (hit is not None and hit[0] == getattr(cache, "metadata_epoch", None) and hit[1] == device
             and hit[2] == request_ids and hit[3] == positions):
         return hit[4]
     return None
 
 
 def clear_metadata_cache(cache) -> None:
-    """Drop the device copies of block tables and slots kept on ``cache``."""
+    """Drop the device copies of block tables, lengths and slots kept on ``cache``."""
     store = getattr(cache, "_psb_metadata", None)
     if store is not None:
         store.clear()
     last = getattr(cache, "_psb_last", None)
     if last is not None:
         last.clear()
+    if getattr(cache, "_psb_table", None) is not None:
+        cache._psb_table = None
 
 
 def _host_metadata(cache, request_ids, positions, device):
@@ -112,21 +115,32 @@ def _build_metadata(cache, request_ids, positions, device):
     if hasattr(cache, "gather_tables"):
         # this package's PagedKVCache: vectorised over its table store, the
         # table gathered straight into pinned memory as [table (B x W) | lengths (B)]
-        rows = cache.table_store_rows(request_ids)
-        counts = cache.store_token_counts(rows)
-        pos = np.asarray(positions, dtype=np.int64)
-        bad = np.flatnonzero((pos < 0) | (pos >= counts))
-        if bad.size:
-            row = int(bad[0])
-            raise ValueError(f"Invalid position {positions[row]} for {request_ids[row]}")
         b = len(request_ids)
-        width = cache.table_width(rows)
-        host = torch.empty(b * (width + 1), dtype=torch.int32, pin_memory=device.type == "cuda")
-        flat = host.numpy()
-        cache.gather_tables(rows, flat, width)
-        flat[b * width:] = pos + 1
-        dev = host.to(device, non_blocking=True)
-        return _Meta(dev[: b * width].view(b, width), dev[b * width:], width)
+        pos = np.fromiter(positions, dtype=np.int64, count=b)
+        pin = device.type == "cuda"
+        table = _table_for(cache, request_ids, device)
+        if table is None:
+            # the batch's device table, kept per (epoch, request list): within
+            # an epoch the blocks do not change (the scheduler reserves a
+            # request's whole capacity when it admits it), so the decode
+            # iterations that follow rebuild only the lengths
+            rows = cache.table_store_rows(request_ids)
+            counts = cache.store_token_counts(rows)
+            _check_positions(pos, counts, positions, request_ids)
+            width = cache.table_width(rows)
+            host = torch.empty(b * (width + 1), dtype=torch.int32, pin_memory=pin)
+            flat = host.numpy()
+            cache.gather_tables(rows, flat, width)
+            flat[b * width:] = pos + 1
+            dev = host.to(device, non_blocking=True)
+            tables = dev[: b * width].view(b, width)
+            cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts)
+            return _Meta(tables, dev[b * width:], width)
+        tables, width, rows, counts = table
+        _check_positions(pos, counts, positions, request_ids)
+        host = torch.empty(b, dtype=torch.int32, pin_memory=pin)
+        host.numpy()[:] = pos + 1
+        return _Meta(tables, host.to(device, non_blocking=True), width)
     else:
         # any cache with the reference's interface
         lengths = np.empty(len(request_ids), dtype=np.int32)
@@ -147,6 +161,23 @@ def _build_metadata(cache, request_ids, positions, device):
         host = host.pin_memory()
     dev = host.to(device, non_blocking=True)
     return _Meta(dev[:, :width], dev[:, width].contiguous(), width)
+
+
+def _table_for(cache, request_ids, device):
+    """(tables, width, store rows, token counts) built earlier in this epoch
+    for this request list on this device, or None."""
+    kept = getattr(cache, "_psb_table", None)
+    if kept is None or kept[0] != cache.metadata_epoch or kept[1] != device or kept[2] != request_ids:
+        return None
+    return kept[3:]
+
+
+def _check_positions(pos: np.ndarray, counts: np.ndarray, positions, request_ids) -> None:
+    """The reference's position check (triton_paged_decode.py:136-139), vectorised."""
+    bad = np.flatnonzero((pos < 0) | (pos >= counts))
+    if bad.size:
+        row = int(bad[0])
+        raise ValueError(f"Invalid position {positions[row]} for {request_ids[row]}")
 
 
 class _Meta:

@@ -207,6 +207,7 @@ class PagedKVCache:
         self._store_tokens = np.zeros(16, dtype=np.int64)   # token count per store row
         self._free_rows: list[int] = []
         self._rows_used = 0
+        self._row_of: dict[str, int] = {}  # live request -> its table-store row
 
     # -- allocation ---------------------------------------------------------
     def allocate(self, request_id: str, num_tokens: int) -> None:
@@ -218,6 +219,7 @@ class PagedKVCache:
         table = BlockTable()
         table._owner = self
         table._row = self._store_row()
+        self._row_of[request_id] = table._row
         for blk in blocks:
             table.append(blk)
         self._tables[request_id] = table
@@ -246,6 +248,7 @@ class PagedKVCache:
         table = self._tables.pop(request_id)
         self._store_clear(table._row)
         self._free_rows.append(table._row)
+        del self._row_of[request_id]
         table._owner, table._row = None, -1
         del self._counts[request_id]
         self.block_manager.free(request_id)
@@ -279,14 +282,10 @@ class PagedKVCache:
         self._store_tokens[row] = 0
 
     def _rows_of(self, request_ids) -> np.ndarray:
-        rows = np.empty(len(request_ids), dtype=np.int64)
-        tables = self._tables
-        for i, r in enumerate(request_ids):
-            t = tables.get(r)
-            if t is None:
-                raise KeyError(f"Unknown request: {r!r}")
-            rows[i] = t._row
-        return rows
+        try:  # one C-level pass over the id -> row map
+            return np.fromiter(map(self._row_of.__getitem__, request_ids), dtype=np.int64, count=len(request_ids))
+        except KeyError as e:
+            raise KeyError(f"Unknown request: {e.args[0]!r}") from None
 
     # -- queries ---------------------------------------------------------------
     def get_block_table(self, request_id: str) -> BlockTable:

@@ -237,11 +237,14 @@ def test_host_metadata_reused_within_an_epoch():
     assert t1 is t2 and l1 is l2 and w1 == w2 == 3
     assert l1.tolist() == [5, 9]
     assert t1.tolist() == [c.get_block_table("x").get_blocks() + [0], c.get_block_table("y").get_blocks()]
-    t3, l3, _ = attention._host_metadata(c, ["x", "y"], [3, 8], dev)   # other positions
-    assert t3 is not t1 and l3.tolist() == [4, 9]
+    t3, l3, _ = attention._host_metadata(c, ["x", "y"], [3, 8], dev)   # other positions, same epoch:
+    assert t3 is t1 and l3 is not l1 and l3.tolist() == [4, 9]          # the table is kept, lengths rebuilt
     c.append_tokens("x", 4)                                             # new epoch
     t4, l4, w4 = attention._host_metadata(c, ["x", "y"], [8, 8], dev)
-    assert w4 == 3 and l4.tolist() == [9, 9] and t4.tolist()[0] == c.get_block_table("x").get_blocks()
+    assert t4 is not t1 and w4 == 3 and l4.tolist() == [9, 9]
+    assert t4.tolist()[0] == c.get_block_table("x").get_blocks()
+    t5, _, _ = attention._host_metadata(c, ["y", "x"], [8, 8], dev)    # another request list
+    assert t5 is not t4 and t5.tolist()[1] == t4.tolist()[0]
     with pytest.raises(ValueError, match="Invalid position"):
         attention._host_metadata(c, ["x", "y"], [9, 8], dev)
     attention.clear_metadata_cache(c)
