@@ -910,6 +910,7 @@ def run_b200(args, world, rank, local):
     # lengths; the block table stays on the device while the cache epoch and
     # the request list do not change.
     iter_positions = [[p - k for p in positions] for k in range(4)]
+    host_us = [0.0, 0.0]  # host time in the API call: first layer call of an iteration, the others
 
     def e2e_step(s, first_iteration):
         i, layer = s % 2, s % LAYERS
@@ -923,7 +924,9 @@ def run_b200(args, world, rank, local):
         # step s - 2's output: its read-back precedes ev_in[i] on the copy stream
         o_keep[i] = None
         qd, kd, vd = views[i]
+        h0 = time.perf_counter()
         o_keep[i] = paged_decode_attention_with_write(qd, kd, vd, cache, ids, pos, layer)
+        host_us[0 if layer == 0 else 1] += 1e6 * (time.perf_counter() - h0)
         ev_done[i].record(compute)
 
     def e2e_run(n, first_iteration):
@@ -948,9 +951,12 @@ def run_b200(args, world, rank, local):
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    host_us[:] = [0.0, 0.0]
+    h_start = time.perf_counter()
     e_start.record(compute)
     e2e_run(e2e_steps, 1)
     e_end.record(compute)
+    host_loop_us = 1e6 * (time.perf_counter() - h_start) / e2e_steps
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
@@ -1017,6 +1023,9 @@ def run_b200(args, world, rank, local):
                          "decode_only_note": "decode + combine without the new-token store, same graphs"},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
+                    "host_us_per_step": round(host_loop_us, 1),
+                    "api_host_us": {"first_call_of_iteration": round(host_us[0] / (e2e_steps // LAYERS), 1),
+                                    "other_calls": round(host_us[1] / (e2e_steps - e2e_steps // LAYERS), 1)},
                     "path": "per layer call: q, new k, new v copied from one pinned host staging buffer, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
                             "one launch), output copied back to pinned host memory; the read-back of step s - 1 "

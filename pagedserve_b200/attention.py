@@ -38,6 +38,7 @@ _KEEP = 4  # metadata entries kept per cache (one per live batch shape)
 
 # triton_paged_decode.py:106-107 raises exactly this text for a host query
 _CUDA_REQUIRED = "Triton paged attention requires CUDA"
+_QUERY_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
 
 def _memo(cache, kind: str, request_ids, positions, device, build):
@@ -50,7 +51,7 @@ def _memo(cache, kind: str, request_ids, positions, device, build):
     epoch = getattr(cache, "metadata_epoch", None)
     if epoch is None:
         return build()
-    dev = device
+    dev = _dev_key(device)
     lists = type(request_ids) is list and type(positions) is list
     last = getattr(cache, "_psb_last", None)
     if last is None:
@@ -77,14 +78,23 @@ def _memo(cache, kind: str, request_ids, positions, device, build):
     return value
 
 
-def _last_hit(cache, kind: str, request_ids, positions, device):
+def _dev_key(device) -> int:
+    """A device as a plain integer (CUDA index, -1 for the CPU): cheap to compare."""
+    if isinstance(device, int):
+        return device
+    return device.index if device.type == "cuda" and device.index is not None else (
+        torch.cuda.current_device() if device.type == "cuda" else -1)
+
+
+def _last_hit(cache, kind: str, request_ids, positions, dev: int):
     """The metadata the last call of this kind built for the same epoch,
-    request list and positions, or None (two list comparisons)."""
+    request list and positions on device index ``dev``, or None (two list
+    comparisons)."""
     last = getattr(cache, "_psb_last", None)
     if last is None or type(request_ids) is not list or type(positions) is not list:
         return None
     hit = last.get(kind)
-    if (hit is not None and hit[0] == getattr(cache, "metadata_epoch", None) and hit[1] == device
+    if (hit is not None and hit[0] == getattr(cache, "metadata_epoch", None) and hit[1] == dev
             and hit[2] == request_ids and hit[3] == positions):
         return hit[4]
     return None
@@ -117,7 +127,6 @@ def _build_metadata(cache, request_ids, positions, device):
         # table gathered straight into pinned memory as [table (B x W) | lengths (B)]
         b = len(request_ids)
         pos = np.fromiter(positions, dtype=np.int64, count=b)
-        pin = device.type == "cuda"
         table = _table_for(cache, request_ids, device)
         if table is None:
             # the batch's device table, kept per (epoch, request list): within
@@ -128,19 +137,22 @@ def _build_metadata(cache, request_ids, positions, device):
             counts = cache.store_token_counts(rows)
             _check_positions(pos, counts, positions, request_ids)
             width = cache.table_width(rows)
-            host = torch.empty(b * (width + 1), dtype=torch.int32, pin_memory=pin)
+            host, done = _staging(cache, b * (width + 1), device)
             flat = host.numpy()
             cache.gather_tables(rows, flat, width)
             flat[b * width:] = pos + 1
             dev = host.to(device, non_blocking=True)
+            done()
             tables = dev[: b * width].view(b, width)
             cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts)
             return _Meta(tables, dev[b * width:], width)
         tables, width, rows, counts = table
         _check_positions(pos, counts, positions, request_ids)
-        host = torch.empty(b, dtype=torch.int32, pin_memory=pin)
+        host, done = _staging(cache, b, device)
         host.numpy()[:] = pos + 1
-        return _Meta(tables, host.to(device, non_blocking=True), width)
+        dev = host.to(device, non_blocking=True)
+        done()
+        return _Meta(tables, dev, width)
     else:
         # any cache with the reference's interface
         lengths = np.empty(len(request_ids), dtype=np.int32)
@@ -161,6 +173,35 @@ def _build_metadata(cache, request_ids, positions, device):
         host = host.pin_memory()
     dev = host.to(device, non_blocking=True)
     return _Meta(dev[:, :width], dev[:, width].contiguous(), width)
+
+
+def _staging(cache, n: int, device):
+    """An int32 host buffer of ``n`` elements for a metadata upload, and the
+    function to call once its copy has been issued.
+
+    For a CUDA device: pinned memory from a ring of two buffers kept on the
+    cache object (pinning memory costs far more than the copy); a buffer is
+    reused only after the copy issued from it has completed (an event)."""
+    if device.type != "cuda":
+        return torch.empty(n, dtype=torch.int32), (lambda: None)
+    ring = getattr(cache, "_psb_staging", None)
+    if ring is None:
+        ring = cache._psb_staging = [[None, None], [None, None], 0]  # [buffer, event] x 2, next slot
+    slot = ring[2]
+    ring[2] = 1 - slot
+    buf, ev = ring[slot]
+    if ev is not None:
+        ev.synchronize()  # normally long complete: the slot was used an iteration ago
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 2 * (buf.numel() if buf is not None else 0)), dtype=torch.int32, pin_memory=True)
+        ring[slot][0] = buf
+
+    def done():
+        e = torch.cuda.Event()
+        e.record(torch.cuda.current_stream(device))
+        ring[slot][1] = e
+
+    return buf[:n], done
 
 
 def _table_for(cache, request_ids, device):
@@ -225,31 +266,34 @@ def _validated_metadata(query, cache, request_ids, positions, layer):
         # the reference wrapper's message, word for word: callers that match
         # on it keep working when this backend replaces the Triton one
         raise ValueError(_CUDA_REQUIRED)
-    if query.ndim != 4 or query.shape[2] != 1:
+    shape = query.shape
+    if len(shape) != 4 or shape[2] != 1:
         raise ValueError("query must have shape [B, Hq, 1, D]")
-    if query.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+    dtype = query.dtype
+    if dtype not in _QUERY_DTYPES:
         raise ValueError("Unsupported query dtype")
-    batch, q_heads, _, head_dim = query.shape
+    batch, q_heads, _, head_dim = shape
     kv = cache.kv_cache
-    kv_heads = kv.num_kv_heads
     if batch == 0:
         raise ValueError("Batch must not be empty")
     if len(request_ids) != batch or len(positions) != batch:
         raise ValueError("Request IDs and positions must match batch size")
+    dev = query.get_device()
     # the metadata of an earlier call with these very lists was built only
     # after they passed every check here, uniqueness included
-    meta = _last_hit(cache, "table", request_ids, positions, query.device)
+    meta = _last_hit(cache, "table", request_ids, positions, dev)
     if meta is None and len(set(request_ids)) != batch:
         raise ValueError("Request IDs must be unique")
     if head_dim != kv.head_dim:
         raise ValueError("Head dimension mismatch")
-    if q_heads % kv_heads:
+    if q_heads % kv.num_kv_heads:
         raise ValueError("Query heads must be divisible by KV heads")
-    if query.dtype != kv.dtype:
+    if dtype != kv.dtype:
         raise ValueError("Query dtype must match cache dtype")
-    if query.device != kv.k_cache.device:
+    k_cache = kv.k_cache
+    if dev != k_cache.get_device():
         raise ValueError("Query and cache must be on the same device")
-    if not 0 <= layer < kv.k_cache.shape[0]:
+    if not 0 <= layer < k_cache.shape[0]:
         raise ValueError("Invalid layer")
     if meta is None:
         meta = _host_metadata(cache, request_ids, positions, query.device)
@@ -282,7 +326,8 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     if key.shape[0] != query.shape[0] or value.shape[0] != query.shape[0]:
         raise ValueError("Request IDs and positions must match batch size")
     meta = _validated_metadata(query, cache, request_ids, positions, layer)
-    if key.device != query.device or value.device != query.device:
+    dev = query.get_device()
+    if key.get_device() != dev or value.get_device() != dev:
         raise ValueError("new K/V must be on the query's device")
     return _launch(meta, cache, query, layer, key, value)
 
