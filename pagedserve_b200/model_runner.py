@@ -241,3 +241,35 @@ class PagedModelRunner:
         def attend(q_rot, k_rot, v, layer):
             return ops.varlen_prefill(q_rot, k_rot, v, cu_seqlens, max_seqlen, scale=self.scale)
         return self._layers(tokens, positions, slots, attend, want_keys=True, last_rows=last_rows)
+
+    # -- prefill and decode in one pass --------------------------------------------
+    def mixed(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, prefill_tokens: int,
+              prefill_cu: torch.Tensor, max_seqlen: int, block_tables: torch.Tensor, context_lens: torch.Tensor,
+              last_rows: torch.Tensor, max_context: int | None = None) -> torch.Tensor:
+        """One engine step's prompts and decode rows in ONE pass.
+
+        Rows ``0 .. prefill_tokens - 1`` of ``tokens, positions, slots`` are
+        prompts packed back to back (``prefill_cu [S+1]``, causal within each,
+        starting at position 0), the remaining ``B`` rows one decode token per
+        running request (``block_tables [B, W]``, ``context_lens [B]`` =
+        position + 1).  Every row goes through the same embedding, norms,
+        projections, RoPE + KV write and MLP launches; only the attention
+        splits: ``varlen_prefill`` over the prompt rows, ``paged_decode`` over
+        the decode rows.  Returns the logits of ``last_rows`` (each prompt's
+        last row, then the decode rows).  Equal, row for row, to ``prefill``
+        and ``decode`` run apart: rows never read each other outside the
+        attention."""
+        tp = int(prefill_tokens)
+        max_context = block_tables.shape[1] * self.block_size if max_context is None else max_context
+
+        def attend(q_rot, k_rot, v, layer):
+            out = torch.empty_like(q_rot)
+            if tp > 0:
+                ops.varlen_prefill(q_rot[:tp], k_rot[:tp], v[:tp], prefill_cu, max_seqlen, scale=self.scale,
+                                   out=out[:tp])
+            if q_rot.shape[0] > tp:
+                ops.paged_decode(q_rot[tp:], self.k_cache, self.v_cache, block_tables, context_lens, layer,
+                                 scale=self.scale, out=out[tp:], max_context=max_context)
+            return out
+        return self._layers(tokens, positions, slots, attend, want_keys=True, last_rows=last_rows)
+

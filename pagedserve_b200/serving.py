@@ -141,24 +141,34 @@ def _bucket(buckets: list[int], n: int) -> int:
 
 
 class _StepGraph:
-    """Static buffers + one captured step.  The plan rows (device int32) are
-    [store row, first new position, new tokens] per entry, plus, for a
-    prefill, each entry's generation budget."""
+    """Static buffers + one captured step.
 
-    def __init__(self, engine: "ReplicaEngine", entries: int, tokens: int, prefill: bool):
+    A decode step has ``entries`` decode rows.  A mixed step has
+    ``prefill_entries`` prompt entries (admitted prompts, then pad sequences
+    filling ``prefill_tokens``) followed by ``entries - prefill_entries``
+    decode rows; its tokens are the prompt tokens then one per decode row.
+    The plan rows (device int32) are [store row, first new position, new
+    tokens, generation budget] per entry (the budget is read for prompt
+    entries only; decode rows keep theirs on the device)."""
+
+    def __init__(self, engine: "ReplicaEngine", entries: int, prefill_entries: int = 0, prefill_tokens: int = 0):
         dev = engine.device
-        self.entries, self.tokens, self.prefill = entries, tokens, prefill
-        nplan = 4 if prefill else 3
-        self.plan_host = torch.zeros((nplan, entries), dtype=torch.int32).pin_memory()
-        self.plan = torch.zeros((nplan, entries), dtype=torch.int32, device=dev)
-        self.tok_host = torch.zeros(tokens, dtype=torch.int64).pin_memory() if prefill else None
-        self.tok_in = torch.zeros(tokens, dtype=torch.int64, device=dev) if prefill else None
+        self.entries, self.prefill_entries, self.prefill_tokens = entries, prefill_entries, prefill_tokens
+        self.decode_rows = entries - prefill_entries
+        self.tokens = prefill_tokens + self.decode_rows
+        self.mixed = prefill_entries > 0
+        self.plan_host = torch.zeros((4, entries), dtype=torch.int32).pin_memory()
+        self.plan = torch.zeros((4, entries), dtype=torch.int32, device=dev)
+        self.tok_host = torch.zeros(max(prefill_tokens, 1), dtype=torch.int64).pin_memory() if self.mixed else None
+        self.tok_in = torch.zeros(self.tokens, dtype=torch.int64, device=dev) if self.mixed else None
         w = engine.table_width
         self.meta = (torch.zeros(entries + 1, dtype=torch.int32, device=dev),
                      torch.zeros(entries, dtype=torch.int32, device=dev),
-                     torch.zeros(tokens, dtype=torch.int64, device=dev),
-                     torch.zeros(tokens, dtype=torch.int64, device=dev),
+                     torch.zeros(self.tokens, dtype=torch.int64, device=dev),
+                     torch.zeros(self.tokens, dtype=torch.int64, device=dev),
                      torch.zeros((entries, w), dtype=torch.int32, device=dev))
+        # rows of the logits: each prompt entry's last token, then every decode row
+        self.decode_last = torch.arange(prefill_tokens, self.tokens, dtype=torch.int64, device=dev)
         self.tok_out = torch.zeros(entries, dtype=torch.int64, device=dev)
         self.status = torch.zeros(entries, dtype=torch.uint8, device=dev)
         self.out_host = torch.zeros(entries * 9, dtype=torch.uint8).pin_memory()
@@ -170,14 +180,18 @@ class _StepGraph:
                       error_flag=e.err, out=self.meta)
         cu, ctx, slots, pos, tables = self.meta
         rows = plan[0].long()
-        if self.prefill:
-            e.remaining.index_copy_(0, rows, plan[3])
-            last = (cu[1:] - 1).clamp_(min=0).long()
-            logits = e.runner.prefill(self.tok_in, pos, slots, cu, e.max_prompt, last)
+        rem = e.remaining.index_select(0, rows)
+        max_context = e.table_width * e.block_size
+        if self.mixed:
+            ep = self.prefill_entries
+            rem[:ep].copy_(plan[3][:ep])  # the admitted requests' budgets
+            self.tok_in[self.prefill_tokens:].copy_(e.last_token.index_select(0, rows[ep:]))
+            last = torch.cat([(cu[1:ep + 1] - 1).clamp_(min=0).long(), self.decode_last])
+            logits = e.runner.mixed(self.tok_in, pos, slots, self.prefill_tokens, cu[:ep + 1], e.max_prompt,
+                                    tables[ep:], ctx[ep:], last, max_context=max_context)
         else:
             tokens_in = e.last_token.index_select(0, rows)
-            logits = e.runner.decode(tokens_in, pos, tables, ctx, slots, max_context=e.table_width * e.block_size)
-        rem = e.remaining.index_select(0, rows)
+            logits = e.runner.decode(tokens_in, pos, tables, ctx, slots, max_context=max_context)
         ops.select_tokens(logits, e.eos, rem, tokens=self.tok_out, status=self.status, error_flag=e.err)
         e.last_token.index_copy_(0, rows, self.tok_out)
         e.remaining.index_copy_(0, rows, rem)
@@ -198,8 +212,8 @@ class _StepGraph:
         """Upload the plan (and prompt tokens), replay, read tokens and status back."""
         stream = torch.cuda.current_stream(e.device)
         self.plan.copy_(self.plan_host, non_blocking=True)
-        if self.prefill:
-            self.tok_in.copy_(self.tok_host, non_blocking=True)
+        if self.mixed:
+            self.tok_in[: self.prefill_tokens].copy_(self.tok_host[: self.prefill_tokens], non_blocking=True)
         self.graph.replay()
         n = self.entries
         out = self.out_host
@@ -215,7 +229,8 @@ class ReplicaEngine:
     def __init__(self, weights: QwenWeights, num_blocks: int, *, block_size: int = 16, max_running: int = 256,
                  max_prefill_tokens: int = 16384, max_prefill_seqs: int = 32, max_prompt: int = 8192,
                  max_context: int = 32768, eos_ids=(), decode_buckets=(64, 128, 256),
-                 prefill_buckets=(512, 1024, 2048, 4096, 8192, 16384), record_tokens: bool = False, free_order=None):
+                 prefill_buckets=(256, 512, 1024, 1536, 2048, 3072, 4096, 6144, 8192, 12288, 16384),
+                 record_tokens: bool = False, free_order=None):
         cfg: QwenConfig = weights.cfg
         self.cfg, self.device = cfg, weights.device
         self.block_size = block_size
@@ -246,9 +261,12 @@ class ReplicaEngine:
         self.prefill_buckets = sorted(prefill_buckets)
         if self.prefill_buckets[-1] < max_prefill_tokens:
             raise ValueError("the largest prefill bucket must hold max_prefill_tokens")
-        self._decode = {b: _StepGraph(self, b, b, prefill=False) for b in self.decode_buckets}
-        self._prefill = {t: _StepGraph(self, max_prefill_seqs + -(-t // PAD_TOKENS), t, prefill=True)
-                         for t in self.prefill_buckets}
+        self._decode = {b: _StepGraph(self, b) for b in self.decode_buckets}
+        # a step with admissions: its prompts (padded to the bucket) and up to
+        # max_running decode rows in one pass
+        self._mixed = {t: _StepGraph(self, max_prefill_seqs + -(-t // PAD_TOKENS) + max_running,
+                                     max_prefill_seqs + -(-t // PAD_TOKENS), t)
+                       for t in self.prefill_buckets}
         # per store row: the request there, its prompt length, tokens generated, decoding or not
         self._req_by_row: list[ServeRequest | None] = [None] * rows
         self._prompt_len = np.zeros(rows, dtype=np.int32)
@@ -261,7 +279,7 @@ class ReplicaEngine:
     def capture(self, decode: bool = True, prefill: bool = True) -> None:
         """Capture every bucket's graph (before serving; the first replay of
         each would otherwise pay for it)."""
-        graphs = (list(self._decode.values()) if decode else []) + (list(self._prefill.values()) if prefill else [])
+        graphs = (list(self._decode.values()) if decode else []) + (list(self._mixed.values()) if prefill else [])
         for g in graphs:
             self._fill_pad_plan(g)
             g.plan.copy_(g.plan_host)
@@ -269,7 +287,7 @@ class ReplicaEngine:
         self.remaining[self.pad_row] = _BIG_REMAINING
 
     def release(self) -> None:
-        for g in list(self._decode.values()) + list(self._prefill.values()):
+        for g in list(self._decode.values()) + list(self._mixed.values()):
             if g.graph is not None:
                 g.graph.reset()
                 g.graph = None
@@ -286,23 +304,35 @@ class ReplicaEngine:
         dev = host.to(self.device, non_blocking=True)
         self.table_store.index_copy_(0, torch.tensor(rows, dtype=torch.int64).to(self.device, non_blocking=True), dev)
 
-    def _fill_pad_plan(self, g: _StepGraph, used_entries: int = 0, used_tokens: int = 0) -> None:
-        """Entries past the real ones: the pad row; a prefill's spare tokens
-        become pad sequences of at most PAD_TOKENS tokens."""
+    def _pad_decode(self, p: np.ndarray, first: int, last: int) -> None:
+        """Decode entries ``first .. last - 1`` that carry no request: one
+        token of the pad request at position 0."""
+        p[0, first:last] = self.pad_row
+        p[1, first:last] = 0
+        p[2, first:last] = 1
+        p[3, first:last] = _BIG_REMAINING
+
+    def _pad_prefill(self, p: np.ndarray, g: _StepGraph, used_entries: int, used_tokens: int) -> None:
+        """Prompt entries past the admitted ones: the bucket's spare tokens as
+        pad-request sequences of at most PAD_TOKENS tokens, then empty ones."""
+        ep = g.prefill_entries
+        p[0, used_entries:ep] = self.pad_row
+        p[1, used_entries:ep] = 0
+        p[2, used_entries:ep] = 0
+        p[3, used_entries:ep] = _BIG_REMAINING
+        spare, e = g.prefill_tokens - used_tokens, used_entries
+        while spare > 0:
+            n = min(spare, PAD_TOKENS)
+            p[2, e] = n
+            spare -= n
+            e += 1
+
+    def _fill_pad_plan(self, g: _StepGraph) -> None:
+        """A plan of padding only (for the capture's warm-up run)."""
         p = g.plan_host.numpy()
-        p[0, used_entries:] = self.pad_row
-        p[1, used_entries:] = 0
-        if g.prefill:
-            p[3, used_entries:] = _BIG_REMAINING
-            spare, e = g.tokens - used_tokens, used_entries
-            p[2, used_entries:] = 0
-            while spare > 0:
-                n = min(spare, PAD_TOKENS)
-                p[2, e] = n
-                spare -= n
-                e += 1
-        else:
-            p[2, used_entries:] = 1
+        if g.mixed:
+            self._pad_prefill(p, g, 0, 0)
+        self._pad_decode(p, g.prefill_entries, g.entries)
 
     # -- serving ----------------------------------------------------------------
     def submit(self, req: ServeRequest) -> None:
@@ -313,23 +343,40 @@ class ReplicaEngine:
         return bool(self.scheduler.waiting or self.scheduler.running)
 
     def step(self) -> list[ServeRequest]:
-        """Admit, prefill the admitted prompts as one pack, decode every
-        running request one token.  Returns the requests that finished."""
-        finished: list[ServeRequest] = []
+        """Admit, then one pass for every running request: the admitted
+        prompts prefilled (packed) and every request already decoding one
+        token, in the same launches.  Returns the requests that finished.
+
+        The reference prefills the admitted requests and then decodes every
+        running one, a new request taking its first decode token in the same
+        iteration (continuous_batcher.py:261-364); here a new request takes
+        its first (prefill) token this step and decodes from the next, so
+        every request's token sequence is the same."""
         admitted = self.scheduler.schedule()
-        if admitted:
-            finished += self._prefill_step(admitted)
         rows = np.flatnonzero(self._decoding).astype(np.int32)
-        if rows.size:
-            finished += self._decode_step(rows)
+        if admitted:
+            finished = self._mixed_step(admitted, rows)
+        elif rows.size:
+            finished = self._decode_step(rows)
+        else:
+            finished = []
         self.stats["steps"] += 1
         return finished
 
-    def _prefill_step(self, admitted: list[ServeRequest]) -> list[ServeRequest]:
+    def _decode_plan(self, p: np.ndarray, at: int, rows: np.ndarray) -> None:
+        n = rows.size
+        p[0, at:at + n] = rows
+        # the token fed sits at num_prompt + num_generated - 1 (continuous_batcher.py:316-319)
+        p[1, at:at + n] = self._prompt_len[rows] + self._generated[rows] - 1
+        p[2, at:at + n] = 1
+
+    def _mixed_step(self, admitted: list[ServeRequest], rows_dec: np.ndarray) -> list[ServeRequest]:
         ids = [r.request_id for r in admitted]
         self._upload_tables(ids)
         total = sum(r.num_prompt_tokens for r in admitted)
-        g = self._prefill[_bucket(self.prefill_buckets, total)]
+        g = self._mixed[_bucket(self.prefill_buckets, total)]
+        if rows_dec.size > g.decode_rows:
+            raise RuntimeError("more decode rows than the step graph holds")
         p = g.plan_host.numpy()
         toks = g.tok_host.numpy()
         rows = np.empty(len(admitted), dtype=np.int32)
@@ -344,24 +391,30 @@ class ReplicaEngine:
             p[0, i], p[1, i], p[2, i], p[3, i] = row, 0, n, r.max_new_tokens
             toks[at:at + n] = r.prompt_token_ids
             at += n
-        toks[at:] = 0
-        self._fill_pad_plan(g, len(admitted), total)
+        toks[at:g.prefill_tokens] = 0
+        self._pad_prefill(p, g, len(admitted), total)
+        ep = g.prefill_entries
+        self._decode_plan(p, ep, rows_dec)
+        self._pad_decode(p, ep + rows_dec.size, g.entries)
         tokens, status = g.run(self)
         self.stats["prefill_steps"] += 1
         self.stats["prefill_tokens"] += total
         self.stats["first_tokens"] += len(admitted)
+        self.stats["decode_steps"] += 1 if rows_dec.size else 0
+        self.stats["decode_tokens"] += rows_dec.size
+        self.stats["decode_rows"] += g.decode_rows
         self._decoding[rows] = True
-        return self._apply(rows, tokens, status)
+        done = self._apply(rows, tokens[: len(admitted)], status[: len(admitted)])
+        if rows_dec.size:
+            done += self._apply(rows_dec, tokens[ep:ep + rows_dec.size], status[ep:ep + rows_dec.size])
+        return done
 
     def _decode_step(self, rows: np.ndarray) -> list[ServeRequest]:
         n = rows.size
         g = self._decode[_bucket(self.decode_buckets, n)]
         p = g.plan_host.numpy()
-        p[0, :n] = rows
-        # the token fed sits at num_prompt + num_generated - 1 (continuous_batcher.py:316-319)
-        p[1, :n] = self._prompt_len[rows] + self._generated[rows] - 1
-        p[2, :n] = 1
-        self._fill_pad_plan(g, n)
+        self._decode_plan(p, 0, rows)
+        self._pad_decode(p, n, g.entries)
         tokens, status = g.run(self)
         self.stats["decode_steps"] += 1
         self.stats["decode_tokens"] += n

@@ -168,3 +168,45 @@ def test_engine_bf16_serving_geometry():
     assert len(finished) == len(reqs)
     assert all(r.generated == r.max_new_tokens and not r.eos for r in reqs)
     assert eng.stats["decode_tokens"] + eng.stats["first_tokens"] == sum(r.max_new_tokens for r in reqs)
+
+
+def test_mixed_pass_equals_prefill_then_decode_fp32():
+    """One pass over new prompts and decode rows (the serving loop's mixed
+    step) gives the logits and pool rows of a packed prefill and a decode
+    run apart."""
+    from pagedserve_b200.model_runner import PagedModelRunner, QwenWeights
+    model = small_qwen(dtype=torch.float32, seed=11)
+    rng = np.random.default_rng(11)
+    plens = [3, 200, 77]           # prompts
+    dlens = [1, 40, 513, 1200]     # decode rows: contexts including the new token
+    nb = sum(-(-n // 16) for n in plens + dlens) + 4
+    tables = random_tables(rng, plens + dlens, nb)
+    kc, vc = _pools(2, nb, torch.float32, 11)
+    kc2, vc2 = kc.clone(), vc.clone()
+    w = QwenWeights.from_hf(model)
+    apart, together = PagedModelRunner(w, kc, vc), PagedModelRunner(w, kc2, vc2)
+    ptab, dtab = tables[:len(plens)], tables[len(plens):]
+    prompts = torch.tensor(rng.integers(0, 512, sum(plens)), device="cuda")
+    ppos = torch.cat([torch.arange(n, device="cuda") for n in plens])
+    pslots = torch.cat([torch.tensor([t[p // 16] * 16 + p % 16 for p in range(n)], device="cuda")
+                        for t, n in zip(ptab, plens)])
+    cu = torch.tensor([0] + list(np.cumsum(plens)), dtype=torch.int32, device="cuda")
+    dtok = torch.tensor(rng.integers(0, 512, len(dlens)), device="cuda")
+    dpos = torch.tensor([n - 1 for n in dlens], device="cuda")
+    dslots = torch.tensor([t[(n - 1) // 16] * 16 + (n - 1) % 16 for t, n in zip(dtab, dlens)], device="cuda")
+    width = max(len(t) for t in dtab)
+    dtable = torch.zeros(len(dlens), width, dtype=torch.int32, device="cuda")
+    for i, t in enumerate(dtab):
+        dtable[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    dctx = torch.tensor(dlens, dtype=torch.int32, device="cuda")
+    a1 = apart.prefill(prompts, ppos, pslots, cu, max(plens), (cu[1:] - 1).long())
+    a2 = apart.decode(dtok, dpos, dtable, dctx, dslots)
+    tp = int(sum(plens))
+    last = torch.cat([(cu[1:] - 1).long(), torch.arange(tp, tp + len(dlens), device="cuda")])
+    b = together.mixed(torch.cat([prompts, dtok]), torch.cat([ppos, dpos]), torch.cat([pslots, dslots]), tp, cu,
+                       max(plens), dtable, dctx, last)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(b, torch.cat([a1, a2]), rtol=1e-5, atol=1e-5)
+    # the projections of a taller GEMM may sum in another fp32 order
+    torch.testing.assert_close(kc2, kc, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(vc2, vc, rtol=1e-5, atol=1e-5)
