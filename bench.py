@@ -890,19 +890,36 @@ def run_b200(args, world, rank, local):
     o_host = [torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     s_copy = torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_done = [torch.cuda.Event() for _ in range(2)]
     o_keep = [None, None]
+    # The copies and the two events go straight to the CUDA runtime on
+    # explicit streams (cuda-python): the same operations as torch's
+    # copy_/Event/wait_event, at a fraction of their host cost in this
+    # host-bound loop.
+    from cuda.bindings import runtime as cudart
+    k_h2d, k_d2h = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost
+    rt_ok = cudart.cudaError_t.cudaSuccess
+
+    def rt_check(res):
+        if res[0] != rt_ok:
+            raise RuntimeError(f"CUDA runtime call failed: {res[0]}")
+        return res[1] if len(res) > 1 else None
+
+    copy_h, comp_h = s_copy.cuda_stream, compute.cuda_stream
+    ev_in = [rt_check(cudart.cudaEventCreateWithFlags(cudart.cudaEventDisableTiming)) for _ in range(2)]
+    ev_done = [rt_check(cudart.cudaEventCreateWithFlags(cudart.cudaEventDisableTiming)) for _ in range(2)]
+    in_ptr, in_dev_ptr = in_host.data_ptr(), [b.data_ptr() for b in in_dev]
+    in_n, o_n = in_host.numel(), o_host[0].numel() * 2
+    o_host_ptr = [t.data_ptr() for t in o_host]
 
     from pagedserve_b200.attention import clear_metadata_cache
 
     def upload(s):  # step s's inputs into buffer s % 2 (its last reader, step s - 2, is done)
-        in_dev[s % 2].copy_(in_host, non_blocking=True)
-        ev_in[s % 2].record(s_copy)
+        rt_check(cudart.cudaMemcpyAsync(in_dev_ptr[s % 2], in_ptr, in_n, k_h2d, copy_h))
+        rt_check(cudart.cudaEventRecord(ev_in[s % 2], copy_h))
 
     def read_back(s):  # step s's output, once its kernel is done
-        s_copy.wait_event(ev_done[s % 2])
-        o_host[s % 2].copy_(o_keep[s % 2], non_blocking=True)
+        rt_check(cudart.cudaStreamWaitEvent(copy_h, ev_done[s % 2], 0))
+        rt_check(cudart.cudaMemcpyAsync(o_host_ptr[s % 2], o_keep[s % 2].data_ptr(), o_n, k_d2h, copy_h))
 
     # Each decode iteration passes new positions, as a serving loop does: here
     # iteration k decodes at positions ctx - 1 - k (inside each request's
@@ -915,30 +932,24 @@ def run_b200(args, world, rank, local):
     def e2e_step(s, first_iteration):
         i, layer = s % 2, s % LAYERS
         pos = iter_positions[first_iteration + s // LAYERS]
-        torch.cuda.set_stream(s_copy)
         if s >= 1:
             read_back(s - 1)  # also orders the upload below after step s - 1's kernel
         upload(s + 1)
-        torch.cuda.set_stream(compute)
-        compute.wait_event(ev_in[i])
+        rt_check(cudart.cudaStreamWaitEvent(comp_h, ev_in[i], 0))
         # step s - 2's output: its read-back precedes ev_in[i] on the copy stream
         o_keep[i] = None
         qd, kd, vd = views[i]
         h0 = time.perf_counter()
         o_keep[i] = paged_decode_attention_with_write(qd, kd, vd, cache, ids, pos, layer)
         host_us[0 if layer == 0 else 1] += 1e6 * (time.perf_counter() - h0)
-        ev_done[i].record(compute)
+        rt_check(cudart.cudaEventRecord(ev_done[i], comp_h))
 
     def e2e_run(n, first_iteration):
-        torch.cuda.set_stream(s_copy)
         s_copy.wait_stream(compute)
         upload(0)
-        torch.cuda.set_stream(compute)
         for s in range(n):
             e2e_step(s, first_iteration)
-        torch.cuda.set_stream(s_copy)
         read_back(n - 1)
-        torch.cuda.set_stream(compute)
         compute.wait_stream(s_copy)
 
     # one whole decode iteration of warm-up (pinned staging and the metadata
@@ -960,6 +971,8 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
+    for ev in ev_in + ev_done:
+        rt_check(cudart.cudaEventDestroy(ev))
     iterations = e2e_steps // LAYERS  # lengths copies inside the timed region
     h2d = in_host.numel() + 4 * batch * iterations / e2e_steps
     # iteration k attends over ctx - k tokens per request
@@ -1029,8 +1042,9 @@ def run_b200(args, world, rank, local):
                     "path": "per layer call: q, new k, new v copied from one pinned host staging buffer, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
                             "one launch), output copied back to pinned host memory; the read-back of step s - 1 "
-                            "and the upload of step s + 1 (two alternating device input buffers) on one copy "
-                            "stream, overlapping step s's kernel; each iteration's first layer call rebuilds and "
+                            "and the upload of step s + 1 (two alternating device input buffers, cudaMemcpyAsync) "
+                            "on one copy stream, overlapping step s's kernel; each iteration's first layer call "
+                            "rebuilds and "
                             "copies the lengths for its new positions (the block table stays on the device within "
                             f"a cache epoch); timed over 2 whole iterations ({LAYERS} layer calls each) after one "
                             "of warm-up"},
