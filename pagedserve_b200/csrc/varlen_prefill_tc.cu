@@ -17,24 +17,26 @@
 // of warp 4 issues the Q loads and S = Q K^T, one lane of warp 5 the K/V
 // loads and O += P V.  They meet only on mbarriers, so the tensor core works
 // while the softmax runs.  A global step counter across the CTA's tiles
-// drives the 4-stage K/V ring (128-byte swizzle, requested three steps ahead,
-// into the next tile too), the two TMEM S buffers and the barrier phases; Q
-// is double-buffered per tile.  Per key tile (step):
+// drives the 4-stage K/V ring (128-byte swizzle, each stage requested again
+// as soon as P.V of its step is done), the two TMEM S buffers and the
+// barrier phases; Q is double-buffered per tile.  Per key tile (step):
 //   producer: S = Q K^T (four tcgen05.mma, M 128, N 64, K 16; fp32 into one of
-//   two TMEM S buffers) one step ahead of the softmax;
+//   two TMEM S buffers) one step ahead of the softmax, once P.V of the step
+//   that last used the buffer is done;
 //   softmax: thread r loads its row of S, masks keys past its own position or
 //   past the sequence and stores P = exp2(S - m) rounded to the input type
 //   (as the reference rounds the probabilities before P.V,
-//   paged_attention.py:133-137) to its TMEM lane, two keys per column.  m is
-//   a lazily updated row max: only when a row's max grows by more than 2^8 is
-//   the O accumulated so far in TMEM rescaled (so P stays below 256 and most
-//   steps touch no O at all);
+//   paged_attention.py:133-137) over the first half of the same S buffer in
+//   its TMEM lane, two keys per column.  m is a lazily updated row max: only
+//   when a row's max grows by more than 2^8 is the O accumulated so far in
+//   TMEM rescaled (so P stays below 256 and most steps touch no O at all);
 //   producer: O += P V (four tcgen05.mma with P read from TMEM, N 64, V as an
-//   MN-major operand; the first step of a tile overwrites O, which the
-//   softmax warps have read for the previous tile before they got there).
-// P is double-buffered in TMEM: the softmax of step g waits only for the P.V
-// of step g - 2, and the producer issues P.V of step g before waiting for
-// step g - 1's, so the softmax and P.V of consecutive steps overlap.
+//   MN-major operand) into the tile's O buffer; the first step of a tile
+//   overwrites it.
+// Consecutive tiles alternate between two TMEM O buffers, and a tile's output
+// is read and written by the softmax warps after the next tile's first step,
+// so no warp waits for a tile's last P.V at the tile boundary.  The K/V request
+// cursor walks the CTA's whole tile list, kKvAhead steps ahead of P.V.
 // Every mbarrier wait is bounded and each phase is waited for before the
 // barrier can move two phases on; on a timeout a CTA records
 // PSB_DEVERR_TIMEOUT, lets its copies and MMAs in flight land (bounded), frees
@@ -57,8 +59,11 @@ constexpr uint32_t kTile = kBM * kDim * 2;    // bytes of one Q tile (16 KB)
 constexpr uint32_t kKvTile = kBN * kDim * 2;  // bytes of one K or V tile (8 KB)
 constexpr int kKvStages = 4;                  // K/V ring depth
 constexpr int kKvAhead = kKvStages;           // K/V of step g + kKvAhead is requested once P.V of step g is done
-constexpr uint32_t kTmemCols = 256;  // S buffers: cols [0, 64), [64, 128); O: [128, 192); P buffers: [192, 256)
-constexpr uint32_t kSCol = 0, kOCol = 128, kPCol = 192, kPCols = 32;
+// TMEM columns: S buffers [0, 64) and [64, 128) (P of a step overwrites the
+// first 32 columns of its S buffer, two 16-bit values per column); O buffers
+// [128, 192) and [192, 256), one per tile in turn
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kSCol = 0, kOCol = 128;
 constexpr float kRescaleLog2 = 8.f;  // rescale O when a row max grows by more than 2^8
 // dynamic shared memory (1024-byte aligned): Q0 | Q1 | K ring | V ring | barriers | tile tables
 constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 2 * kTile + kKvStages * kKvTile;
@@ -125,12 +130,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + kSmemTiles);  // [2]
   uint64_t* bar_kv = bar_q + 2;                                      // [kKvStages]
   uint64_t* bar_s = bar_q + 2 + kKvStages;                           // [2]
-  uint64_t* bar_sfree = bar_s + 2;  // [2] S buffer read by the softmax
-  uint64_t* bar_pv = bar_sfree + 2;  // [2] P.V of a step using P buffer g & 1 done
+  uint64_t* bar_pv = bar_s + 2;      // [2] P.V of step g (which read P from S buffer g & 1) done
   uint64_t* bar_p = bar_pv + 2;      // [2] softmax step done: P buffer g & 1 written
   uint64_t* bar_qfree = bar_p + 2;   // a tile's Q K^T done
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_qfree + 1);
-  static_assert(15 * sizeof(uint64_t) + sizeof(uint32_t) <= kSmemBars, "barriers fit their area");
+  static_assert(13 * sizeof(uint64_t) + sizeof(uint32_t) <= kSmemBars, "barriers fit their area");
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
   int32_t* s_lstart = reinterpret_cast<int32_t*>(smem + kSmemTiles + kSmemBars);  // [max_level + 1]
   int32_t* s_cnt = s_lstart + (max_level + 1);   // [max_level + 1] sequences with more than i blocks
@@ -256,8 +260,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     for (int i = 0; i < kKvStages; ++i) mbar_init(bar_kv + i, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_s + 1, 1);
-    mbar_init(bar_sfree, kSoftmaxThreads);
-    mbar_init(bar_sfree + 1, kSoftmaxThreads);
     mbar_init(bar_pv, 1);
     mbar_init(bar_pv + 1, 1);
     mbar_init(bar_p, kSoftmaxThreads);
@@ -316,9 +318,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           const int n_kv = tile_of(k).n_kv;
           const uint64_t dqs = dq + static_cast<uint64_t>((k & 1) * (kTile >> 4));
           for (int j = 0; j < n_kv; ++j, ++g) {
-            // S buffer g & 1 held step g - 2: read by the softmax (the next phase
-            // needs this step's S, so the parity cannot alias)
-            if (g >= 2 && !mbar_wait(bar_sfree + (g & 1), ((g - 2) >> 1) & 1)) {
+            // S buffer g & 1 held S and then P of step g - 2: free once that
+            // step's P.V is done (the barrier's next phase needs this step's S,
+            // so the parity cannot alias)
+            if (g >= 2 && !mbar_wait(bar_pv + (g & 1), ((g - 2) >> 1) & 1)) {
               fail = true;
               break;
             }
@@ -347,11 +350,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // V descriptor of stage 0; a stage advances the address field by
         // kKvTile >> 4, a k-step of 16 keys by 2048 >> 4
         const uint64_t dv = umma_desc_sw128(s_base + kOffV, 1024, 8192);
-        TileInfo tc = tile_of(0), tn{};  // current and next tile
-        bool tn_valid = my_tiles > 1;
-        if (tn_valid) tn = tile_of(1);
-        // K/V requests run ahead through the current and the next tile
-        int rk = 0, rj = 0, rg = 0;  // tile (0 current, 1 next), step and global step of the next request
+        // The request cursor walks this CTA's whole tile list (in shared
+        // memory), so requests stay kKvAhead steps ahead across tile ends.
+        int ck = 0, cj = 0, rg = 0;  // tile, step and global step of the next request
+        TileInfo cti = tile_of(0);
         // paged: block ids of the request the cursor points at, loaded while
         // the step before it runs (pf_g: its global step, -1 for none)
         static_assert(kBN / kPoolBlock == 4, "four pool blocks per key step");
@@ -366,39 +368,23 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         };
         auto prefetch_ids = [&]() {
           if constexpr (PAGED) {
-            // the request the cursor points at: step rj of the current tile,
-            // or the first step of the next one
-            int seq = tc.seq, ctx = tc.ctx, j = rj;
-            if (rk == 1 || rj >= tc.n_kv) {
-              if (!tn_valid || (rk == 1 && rj >= tn.n_kv)) return;
-              seq = tn.seq;
-              ctx = tn.ctx;
-              j = rk == 1 ? rj : 0;
-            }
-            pf_ids = load_ids(seq, ctx, j);
+            if (ck >= my_tiles || pf_g == rg) return;
+            pf_ids = load_ids(cti.seq, cti.ctx, cj);
             pf_g = rg;
           }
         };
         auto request_kv = [&](int limit_g) {
-          while (rg <= limit_g) {
-            if (rk == 1 && !tn_valid) break;
-            const TileInfo& ti = rk == 0 ? tc : tn;
-            if (rj >= ti.n_kv) {
-              if (rk == 1) break;  // tiles after the next are not known yet
-              ++rk;
-              rj = 0;
-              continue;
-            }
+          while (rg <= limit_g && ck < my_tiles) {
             const int st = rg % kKvStages;
             if constexpr (PAGED) {
               // the step's four pool blocks; blocks past the context are not
               // loaded (the softmax zeroes their V rows), bad ids are flagged
-              const int nblk = (ti.ctx + kPoolBlock - 1) / kPoolBlock;
-              const int4 id4 = pf_g == rg ? pf_ids : load_ids(ti.seq, ti.ctx, rj);
+              const int nblk = (cti.ctx + kPoolBlock - 1) / kPoolBlock;
+              const int4 id4 = pf_g == rg ? pf_ids : load_ids(cti.seq, cti.ctx, cj);
               int32_t ids[kBN / kPoolBlock] = {id4.x, id4.y, id4.z, id4.w};
 #pragma unroll
               for (int b = 0; b < kBN / kPoolBlock; ++b) {
-                const int idx = rj * (kBN / kPoolBlock) + b;
+                const int idx = cj * (kBN / kPoolBlock) + b;
                 if (idx < nblk && (ids[b] < 0 || ids[b] >= p.num_blocks)) {
                   flag_error(p.err, PSB_DEVERR_BLOCK_RANGE);
                   ids[b] = -1;
@@ -412,37 +398,42 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               for (int b = 0; b < kBN / kPoolBlock; ++b) {
                 if (ids[b] < 0) continue;
                 const int32_t tile = static_cast<int32_t>((static_cast<int64_t>(p.layer) * p.num_blocks + ids[b]) *
-                                                          p.hkv + ti.kvh);
+                                                          p.hkv + cti.kvh);
                 tma_load_3d(smem + kOffK + st * kKvTile + b * kPoolTile, &tm_k, 0, 0, tile, bar_kv + st);
                 tma_load_3d(smem + kOffV + st * kKvTile + b * kPoolTile, &tm_v, 0, 0, tile, bar_kv + st);
               }
             } else {
               mbar_arrive_expect_tx(bar_kv + st, 2 * kKvTile);
-              tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
-              tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, ti.kvh, ti.q0 + rj * kBN, bar_kv + st);
+              tma_load_3d(smem + kOffK + st * kKvTile, &tm_k, 0, cti.kvh, cti.q0 + cj * kBN, bar_kv + st);
+              tma_load_3d(smem + kOffV + st * kKvTile, &tm_v, 0, cti.kvh, cti.q0 + cj * kBN, bar_kv + st);
             }
-            ++rj;
             ++rg;
+            if (++cj >= cti.n_kv) {
+              cj = 0;
+              if (++ck < my_tiles) cti = tile_of(ck);
+            }
           }
         };
         request_kv(kKvAhead - 1);
         int pv_issued = 0, pv_seen = 0, g = 0;
         for (int k = 0; k < my_tiles && !fail; ++k) {
-          const bool has_next = k + 1 < my_tiles;
-          for (int j = 0; j < tc.n_kv && !fail; ++j, ++g) {
+          const int n_kv = tile_of(k).n_kv;
+          const uint32_t obuf = tmem + kOCol + (k & 1) * kDim;  // O buffers alternate between tiles
+          for (int j = 0; j < n_kv && !fail; ++j, ++g) {
             prefetch_ids();  // the next request's block ids land while this step runs
-            // softmax step g done: P buffer g & 1 written (its next phase, step
-            // g + 2, needs P.V of this step first, so the parity cannot alias)
+            // softmax step g done: P written into S buffer g & 1 (the barrier's
+            // next phase, step g + 2, needs P.V of this step first, so the
+            // parity cannot alias)
             if (!mbar_wait(bar_p + (g & 1), (g >> 1) & 1)) {
               fail = true;
               break;
             }
             tc_fence_after();
             const uint64_t dvs = dv + static_cast<uint64_t>((g % kKvStages) * (kKvTile >> 4));
-            const uint32_t pcol = tmem + kPCol + (g & 1) * kPCols;
+            const uint32_t pcol = tmem + kSCol + (g & 1) * kBN;
 #pragma unroll
             for (int kk = 0; kk < kBN / 16; ++kk)
-              umma_f16_ts(tmem + kOCol, pcol + 8 * kk, dvs + 128 * kk, idesc_o, j > 0 || kk > 0);
+              umma_f16_ts(obuf, pcol + 8 * kk, dvs + 128 * kk, idesc_o, j > 0 || kk > 0);
             umma_commit(bar_pv + (g & 1));
             ++pv_issued;
             // the previous step's P.V (done in order before this one) frees its
@@ -455,20 +446,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
               ++pv_seen;
               request_kv(g - 1 + kKvAhead);
             }
-          }
-          if (fail) break;
-          if (has_next) {  // the next tile becomes current
-            tc = tn;
-            if (rk == 1) {
-              rk = 0;
-            } else {  // the cursor had just finished the old tile: start the new one
-              rk = 0;
-              rj = 0;
-            }
-            tn_valid = k + 2 < my_tiles;
-            if (tn_valid) tn = tile_of(k + 2);
-            // the new next tile may take requests now (P.V of step g - 2 was the last seen)
-            request_kv(g - 2 + kKvAhead);
           }
         }
         if (fail) {
@@ -489,10 +466,53 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const float sc = p.scale_log2;
     // output rows 16-byte aligned: whole-row vector stores
     const bool out16 = reinterpret_cast<uintptr_t>(p.out) % 16 == 0 && p.ost % 8 == 0 && p.osh % 8 == 0;
+    // A tile's output is written after the next tile's first step (or at the
+    // end): by then its last P.V is normally done, so the softmax does not
+    // wait for it, and the tensor core has the next tile's work meanwhile.
+    // The next tile accumulates into the other O buffer; the tile after that
+    // overwrites this one only after P of its first step, which this thread
+    // writes after the output below.
+    int pend_k = -1;   // the tile whose output is pending (-1: none)
+    float pend_l = 0.f;  // its row sum
+    // the output of tile pk, whose last step was global step pg
+    auto write_pending = [&](int pk, int pg) -> bool {
+      if (!mbar_wait(bar_pv + (pg & 1), (pg >> 1) & 1)) return false;
+      tc_fence_after();
+      const uint32_t t_po = t_lane + kOCol + (pk & 1) * kDim;
+      uint32_t ot[kDim];
+      tmem_ld32(t_po, ot);
+      tmem_ld32(t_po + 32, ot + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      const TileInfo pt = tile_of(pk);
+      const int prow = pt.qblk * kBM + row;
+      if (prow < pt.len && pt.q0 + prow < p.total) {
+        const float inv = pend_l > 0.f ? 1.f / pend_l : 0.f;
+        T* op = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(pt.q0 + prow) * p.ost +
+                static_cast<int64_t>(pt.head) * p.osh;
+        if (out16) {
+#pragma unroll
+          for (int d = 0; d < kDim; d += 8)
+            *reinterpret_cast<uint4*>(op + d) =
+                make_uint4(pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 2]) * inv, __uint_as_float(ot[d + 3]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 4]) * inv, __uint_as_float(ot[d + 5]) * inv),
+                           pack2<T>(__uint_as_float(ot[d + 6]) * inv, __uint_as_float(ot[d + 7]) * inv));
+        } else {
+#pragma unroll
+          for (int d = 0; d < kDim; d += 2)
+            *reinterpret_cast<uint32_t*>(op + d) =
+                pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
+        }
+      }
+      pend_k = -1;
+      return true;
+    };
     int g = 0;
     for (int k = 0; k < my_tiles && !fail; ++k) {
       const TileInfo ti = tile_of(k);
       const int qrow = ti.qblk * kBM + row;  // position in the sequence
+      const uint32_t t_o = t_lane + kOCol + (k & 1) * kDim;  // this tile's O buffer, this warp's lanes
       float ms = -INFINITY, l_run = 0.f;     // row max used for the exponents (scaled by sc), row sum
       for (int j = 0; j < ti.n_kv; ++j, ++g) {
         if (!mbar_wait(bar_s + (g & 1), (g >> 1) & 1)) {
@@ -504,8 +524,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tmem_ld32(t_lane + kSCol + (g & 1) * kBN, sr);
         tmem_ld32(t_lane + kSCol + (g & 1) * kBN + 32, sr + 32);
         tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(bar_sfree + (g & 1));  // the S buffer may take step g + 2
         if (PAGED && j == ti.n_kv - 1 && row < kBN && j * kBN + row >= ti.ctx) {
           // V rows past the context (stale or never loaded) must not reach
           // P.V, where 0 * NaN would be NaN: zero them before this thread's
@@ -544,13 +562,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             }
             tc_fence_after();
             uint32_t ot[kDim];
-            tmem_ld32(t_lane + kOCol, ot);
-            tmem_ld32(t_lane + kOCol + 32, ot + 32);
+            tmem_ld32(t_o, ot);
+            tmem_ld32(t_o + 32, ot + 32);
             tmem_wait_ld();
 #pragma unroll
             for (int d = 0; d < kDim; ++d) ot[d] = __float_as_uint(__uint_as_float(ot[d]) * alpha);
-            tmem_st32(t_lane + kOCol, ot);
-            tmem_st32(t_lane + kOCol + 32, ot + 32);
+            tmem_st32(t_o, ot);
+            tmem_st32(t_o + 32, ot + 32);
             tmem_wait_st();
           }
           l_run *= alpha;
@@ -571,53 +589,22 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         const float2 rsp = up2(rs2);
         const float rs = rsp.x + rsp.y;
         l_run += rs;
-        // P buffer g & 1 held P of step g - 2: wait for that P.V (normally long
-        // done; P.V of step g cannot start before this thread's arrival below,
-        // so the parity cannot alias)
-        if (g >= 2) {
-          if (!mbar_wait(bar_pv + (g & 1), ((g - 2) >> 1) & 1)) {
-            fail = true;
-            break;
-          }
-        }
-        tmem_st32(t_lane + kPCol + (g & 1) * kPCols, pk);
+        // P over the first half of this step's S buffer (this lane's S is in
+        // registers; the buffer takes S of step g + 2 only after P.V of this step)
+        tmem_st32(t_lane + kSCol + (g & 1) * kBN, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar_p + (g & 1));
-      }
-      if (fail) break;
-      // the tile's last P.V, then its output (before this thread's arrival for
-      // the next tile's first step lets the producer overwrite O)
-      if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) {
-        fail = true;
-        break;
-      }
-      tc_fence_after();
-      uint32_t ot[kDim];
-      tmem_ld32(t_lane + kOCol, ot);
-      tmem_ld32(t_lane + kOCol + 32, ot + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      if (qrow < ti.len && ti.q0 + qrow < p.total) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        T* op = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(ti.q0 + qrow) * p.ost +
-                static_cast<int64_t>(ti.head) * p.osh;
-        if (out16) {
-#pragma unroll
-          for (int d = 0; d < kDim; d += 8)
-            *reinterpret_cast<uint4*>(op + d) =
-                make_uint4(pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 2]) * inv, __uint_as_float(ot[d + 3]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 4]) * inv, __uint_as_float(ot[d + 5]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 6]) * inv, __uint_as_float(ot[d + 7]) * inv));
-        } else {
-#pragma unroll
-          for (int d = 0; d < kDim; d += 2)
-            *reinterpret_cast<uint32_t*>(op + d) =
-                pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
+        if (j == 0 && pend_k >= 0 && !write_pending(pend_k, g - 1)) {  // the previous tile's output
+          fail = true;
+          break;
         }
       }
+      if (fail) break;
+      pend_k = k;
+      pend_l = l_run;
     }
+    if (!fail && pend_k >= 0 && !write_pending(pend_k, g - 1)) fail = true;
     if (fail && lane == 0) flag_error(p.err, PSB_DEVERR_TIMEOUT);
   }
   tc_fence_before();
