@@ -69,6 +69,11 @@ constexpr float kRescaleLog2 = 8.f;  // rescale O when a row max grows by more t
 constexpr uint32_t kOffQ = 0, kOffK = 2 * kTile, kOffV = 2 * kTile + kKvStages * kKvTile;
 constexpr uint32_t kSmemTiles = 2 * kTile + 2 * kKvStages * kKvTile;
 constexpr uint32_t kSmemBars = 128;
+// output staging: per softmax warp, 32 rows x 64 bytes (half a row of the tile
+// at a time), so each global store instruction writes whole row segments
+constexpr uint32_t kOutStageWarp = 32 * 64;
+constexpr uint32_t kOffOut = kSmemTiles + kSmemBars;
+constexpr uint32_t kSmemOut = 4 * kOutStageWarp;
 constexpr int kMaxLevels = 1024;    // query blocks per sequence (128 K tokens)
 constexpr int kMaxTcSeqs = 2048;    // sequences whose order fits the shared tile table
 
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bar_qfree + 1);
   static_assert(13 * sizeof(uint64_t) + sizeof(uint32_t) <= kSmemBars, "barriers fit their area");
   const int max_level = (p.max_seqlen + kBM - 1) / kBM;
-  int32_t* s_lstart = reinterpret_cast<int32_t*>(smem + kSmemTiles + kSmemBars);  // [max_level + 1]
+  int32_t* s_lstart = reinterpret_cast<int32_t*>(smem + kOffOut + kSmemOut);  // [max_level + 1]
   int32_t* s_cnt = s_lstart + (max_level + 1);   // [max_level + 1] sequences with more than i blocks
   int32_t* s_fill = s_cnt + (max_level + 1);     // [max_level + 1] placement cursors
   int32_t* s_sorted = s_fill + (max_level + 1);  // [num_seqs] sequences by query blocks, descending, stable
@@ -479,32 +484,48 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       if (!mbar_wait(bar_pv + (pg & 1), (pg >> 1) & 1)) return false;
       tc_fence_after();
       const uint32_t t_po = t_lane + kOCol + (pk & 1) * kDim;
-      uint32_t ot[kDim];
-      tmem_ld32(t_po, ot);
-      tmem_ld32(t_po + 32, ot + 32);
-      tmem_wait_ld();
-      tc_fence_before();
       const TileInfo pt = tile_of(pk);
       const int prow = pt.qblk * kBM + row;
-      if (prow < pt.len && pt.q0 + prow < p.total) {
-        const float inv = pend_l > 0.f ? 1.f / pend_l : 0.f;
-        T* op = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(pt.q0 + prow) * p.ost +
-                static_cast<int64_t>(pt.head) * p.osh;
+      const float inv = pend_l > 0.f ? 1.f / pend_l : 0.f;
+      const int64_t tok0 = static_cast<int64_t>(pt.q0) + pt.qblk * kBM + warp * 32;  // token of warp row 0
+      T* const out_h = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(pt.head) * p.osh;
+      uint8_t* stg = smem + kOffOut + warp * kOutStageWarp;
+      const int rl = lane >> 2, cl = lane & 3;
+      // half a row (32 columns) at a time
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t ot[32];
+        tmem_ld32(t_po + 32 * h, ot);
+        tmem_wait_ld();
+        uint32_t ob[16];  // the half row rounded to T, two values per word
+#pragma unroll
+        for (int d = 0; d < 32; d += 2)
+          ob[d / 2] = pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
         if (out16) {
+          // through this warp's staging area: lane r writes row r's four
+          // 16-byte chunks (chunk c at slot c ^ ((r >> 1) & 3): no bank
+          // conflicts), then lanes 4 r .. 4 r + 3 store the chunks of row
+          // 8 i + r, so a quarter-warp writes two whole 64-byte segments
 #pragma unroll
-          for (int d = 0; d < kDim; d += 8)
-            *reinterpret_cast<uint4*>(op + d) =
-                make_uint4(pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 2]) * inv, __uint_as_float(ot[d + 3]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 4]) * inv, __uint_as_float(ot[d + 5]) * inv),
-                           pack2<T>(__uint_as_float(ot[d + 6]) * inv, __uint_as_float(ot[d + 7]) * inv));
-        } else {
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)) =
+                make_uint4(ob[4 * c], ob[4 * c + 1], ob[4 * c + 2], ob[4 * c + 3]);
+          __syncwarp();
 #pragma unroll
-          for (int d = 0; d < kDim; d += 2)
-            *reinterpret_cast<uint32_t*>(op + d) =
-                pack2<T>(__uint_as_float(ot[d]) * inv, __uint_as_float(ot[d + 1]) * inv);
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + rl;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 64 + ((cl ^ ((rr >> 1) & 3)) * 16));
+            if (pt.qblk * kBM + warp * 32 + rr < pt.len && tok0 + rr < p.total)
+              *reinterpret_cast<uint4*>(out_h + (tok0 + rr) * p.ost + 32 * h + 8 * cl) = v;
+          }
+          __syncwarp();
+        } else if (prow < pt.len && pt.q0 + prow < p.total) {
+          T* op = out_h + static_cast<int64_t>(pt.q0 + prow) * p.ost + 32 * h;
+#pragma unroll
+          for (int d = 0; d < 32; d += 2) *reinterpret_cast<uint32_t*>(op + d) = ob[d / 2];
         }
       }
+      tc_fence_before();
       pend_k = -1;
       return true;
     };
@@ -514,11 +535,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const int qrow = ti.qblk * kBM + row;  // position in the sequence
       const uint32_t t_o = t_lane + kOCol + (k & 1) * kDim;  // this tile's O buffer, this warp's lanes
       float ms = -INFINITY, l_run = 0.f;     // row max used for the exponents (scaled by sc), row sum
-      for (int j = 0; j < ti.n_kv; ++j, ++g) {
-        if (!mbar_wait(bar_s + (g & 1), (g >> 1) & 1)) {
-          fail = true;
-          break;
-        }
+      // step j of this tile (global step g); false when a wait ran out
+      auto step = [&](int j) -> bool {
+        if (!mbar_wait(bar_s + (g & 1), (g >> 1) & 1)) return false;
         tc_fence_after();
         uint32_t sr[kBN];
         tmem_ld32(t_lane + kSCol + (g & 1) * kBN, sr);
@@ -556,10 +575,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           const float ms_new = grow ? mxs : ms;
           const float alpha = ms == -INFINITY ? 0.f : ex2_approx(ms - ms_new);  // 1 where the max stays
           if (j > 0) {  // O holds P.V of the earlier steps once the last of them is done
-            if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) {
-              fail = true;
-              break;
-            }
+            if (!mbar_wait(bar_pv + ((g - 1) & 1), ((g - 1) >> 1) & 1)) return false;
             tc_fence_after();
             uint32_t ot[kDim];
             tmem_ld32(t_o, ot);
@@ -595,7 +611,21 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar_p + (g & 1));
-        if (j == 0 && pend_k >= 0 && !write_pending(pend_k, g - 1)) {  // the previous tile's output
+        return true;
+      };
+      // The first step, then the previous tile's output (outside the step
+      // loop, whose registers it would otherwise crowd), then the rest.
+      if (!step(0)) {
+        fail = true;
+        break;
+      }
+      if (pend_k >= 0 && !write_pending(pend_k, g - 1)) {
+        fail = true;
+        break;
+      }
+      ++g;
+      for (int j = 1; j < ti.n_kv; ++j, ++g) {
+        if (!step(j)) {
           fail = true;
           break;
         }
@@ -616,7 +646,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 }
 
 size_t tc_smem_bytes(int max_level, int num_seqs, int max_cta_tiles) {
-  return 1024 + kSmemTiles + kSmemBars + sizeof(int32_t) * (3 * (static_cast<size_t>(max_level) + 1) + num_seqs) +
+  return 1024 + kSmemTiles + kSmemBars + kSmemOut +
+         sizeof(int32_t) * (3 * (static_cast<size_t>(max_level) + 1) + num_seqs) +
          16 + 2 * sizeof(int4) * static_cast<size_t>(max_cta_tiles);
 }
 
