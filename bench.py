@@ -757,10 +757,24 @@ def build_device_workload(seed: int, device: torch.device, lens: np.ndarray | No
                 q=q, new_k=new_k, new_v=new_v)
 
 
+def pin_host_cores(world: int, local: int) -> int:
+    """With several ranks on one host, give each its own slice of the allowed
+    cores, in order (on a two-socket board the low ranks' GPUs and the low
+    cores usually share a socket), so the host-bound end-to-end loops of the
+    ranks do not contend or migrate.  Returns the cores this rank keeps."""
+    cpus = sorted(os.sched_getaffinity(0))
+    per = len(cpus) // max(world, 1)
+    if world <= 1 or per < 1:
+        return len(cpus)
+    os.sched_setaffinity(0, cpus[local * per:(local + 1) * per])
+    return per
+
+
 def run_b200(args, world, rank, local):
     from pagedserve_b200 import ops, paged_decode_attention_with_write
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    host_cores = pin_host_cores(world, local)
     pg, host_group = None, None
     if world > 1:
         import datetime
@@ -984,7 +998,8 @@ def run_b200(args, world, rank, local):
     lens = w["lens"]
     step_bytes = decode_bytes(lens) + reshape_bytes(batch)
     rank_step_ms = step_ms
-    per_rank = gather_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "single_ms": single_ms,
+    per_rank = gather_counters({"step_ms": step_ms, "dec_ms": dec_ms, "e2e_ms": e2e_ms, "e2e_host_us": host_loop_us,
+                                "host_cores": host_cores, "single_ms": single_ms,
                                 "two_ms": two_ms, "bytes": step_bytes, "e2e_bytes": e2e_rank_bytes, "seqs": batch,
                                 "ctx": int(lens.sum())}, host_group)
     step_ms, dec_ms, e2e_ms, single_ms, two_ms = (max(r[k] for r in per_rank) for k in
@@ -1017,7 +1032,9 @@ def run_b200(args, world, rank, local):
                 "two_launch_ms": round(two_ms, 5),
                 "two_launch_note": "the step as reshape_and_cache (slot mapping) then decode, same graphs",
                 "per_rank": [{"step_ms": round(r["step_ms"], 5), "sequences": int(r["seqs"]), "sum_ctx": int(r["ctx"]),
-                              "gbs": round(r["bytes"] / (r["step_ms"] * 1e-3) / 1e9, 1)} for r in per_rank],
+                              "gbs": round(r["bytes"] / (r["step_ms"] * 1e-3) / 1e9, 1),
+                              "e2e_ms": round(r["e2e_ms"], 5), "e2e_host_us_per_step": round(r["e2e_host_us"], 1),
+                              "host_cores": int(r["host_cores"])} for r in per_rank],
             },
             "pct_of_8tbs": round(100 * value / world / NOMINAL_HBM_GBS, 2),
             "pct_of_measured_peak": round(100 * value / world / peak, 2),
