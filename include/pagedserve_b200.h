@@ -196,6 +196,48 @@ int psb_paged_decode_append(const void* query, int64_t q_stride_b, int64_t q_str
                             int32_t* error_flag, psb_stream_t stream);
 
 /*
+ * paged_decode_args: psb_paged_decode / psb_paged_decode_append with the
+ * arguments that stay the same for every layer call of one decode iteration
+ * (pools, block table, lengths, geometry, scale, workspace, error flag)
+ * passed as one caller-owned struct, filled once per batch; only the query,
+ * output, new rows, layer and stream are passed per call.  new_key and
+ * new_value both null: psb_paged_decode; both set: psb_paged_decode_append;
+ * one of them null: PSB_ERR_INVALID.  Results, checks and error behaviour
+ * are those of the two calls.  No counterpart in the reference: it exists so
+ * an FFI host pays the marshalling of 14 arguments per layer call instead of
+ * 32 (psb_decode_args_size() gives sizeof(psb_decode_args), for bindings to
+ * check their layout).
+ */
+typedef struct psb_decode_args {
+  void* k_cache;
+  void* v_cache;
+  const int32_t* block_tables;
+  int64_t table_stride;
+  const int32_t* context_lens;
+  int64_t num_blocks;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* error_flag;
+  int32_t batch;
+  int32_t q_heads;
+  int32_t num_layers;
+  int32_t num_kv_heads;
+  int32_t block_size;
+  int32_t head_dim;
+  int32_t dtype;
+  int32_t max_context;
+  float scale;
+  int32_t reserved;  /* zero */
+} psb_decode_args;
+
+size_t psb_decode_args_size(void);
+
+int psb_paged_decode_args(const psb_decode_args* args, const void* query, int64_t q_stride_b, int64_t q_stride_h,
+                          void* out, int64_t o_stride_b, int64_t o_stride_h, const void* new_key,
+                          int64_t key_stride_b, int64_t key_stride_h, const void* new_value,
+                          int64_t value_stride_b, int64_t value_stride_h, int32_t layer, psb_stream_t stream);
+
+/*
  * paged_decode_static: psb_paged_decode without a caller workspace.  It has
  * no counterpart in the reference (whose Triton decode needs no scratch); it
  * exists for callers that cannot allocate device memory where they launch

@@ -29,6 +29,20 @@ DEVERR_BITS = {
 
 _c_void_p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
+
+class DecodeArgs(ctypes.Structure):
+    """``psb_decode_args``: the fixed arguments of psb_paged_decode_args
+    (same fields, order and types as the header; ``load`` checks the size
+    against ``psb_decode_args_size``)."""
+
+    _fields_ = [("k_cache", _c_void_p), ("v_cache", _c_void_p), ("block_tables", _c_void_p),
+                ("table_stride", _i64), ("context_lens", _c_void_p), ("num_blocks", _i64),
+                ("workspace", _c_void_p), ("workspace_bytes", _sz), ("error_flag", _c_void_p),
+                ("batch", _i32), ("q_heads", _i32), ("num_layers", _i32), ("num_kv_heads", _i32),
+                ("block_size", _i32), ("head_dim", _i32), ("dtype", _i32), ("max_context", _i32),
+                ("scale", _f32), ("reserved", _i32)]
+
+
 # name -> (restype, argtypes); mirrors include/pagedserve_b200.h
 SIGNATURES = {
     "psb_version": (ctypes.c_char_p, []),
@@ -54,6 +68,10 @@ SIGNATURES = {
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64,
         _i64, _c_void_p, _i64, _c_void_p, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32,
         _c_void_p, _sz, _c_void_p, _c_void_p]),
+    "psb_decode_args_size": (_sz, []),
+    "psb_paged_decode_args": (ctypes.c_int, [
+        _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64,
+        _i32, _c_void_p]),
     "psb_paged_decode_static": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p, _i32,
         _i32, _i32, _i32, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _c_void_p, _c_void_p]),
@@ -96,6 +114,9 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        if lib.psb_decode_args_size() != ctypes.sizeof(DecodeArgs):
+            raise RuntimeError(f"psb_decode_args is {lib.psb_decode_args_size()} bytes in {LIB_PATH}, "
+                               f"{ctypes.sizeof(DecodeArgs)} in the binding")
         _lib = lib
     return _lib
 

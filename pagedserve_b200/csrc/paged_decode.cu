@@ -1376,6 +1376,22 @@ extern "C" int psb_paged_decode(const void* query, int64_t q_stride_b, int64_t q
                            workspace_bytes, error_flag, stream);
 }
 
+extern "C" size_t psb_decode_args_size(void) { return sizeof(psb_decode_args); }
+
+// The fixed arguments from the caller's struct, the per-call ones as given.
+extern "C" int psb_paged_decode_args(const psb_decode_args* a, const void* query, int64_t q_stride_b,
+                                     int64_t q_stride_h, void* out, int64_t o_stride_b, int64_t o_stride_h,
+                                     const void* new_key, int64_t key_stride_b, int64_t key_stride_h,
+                                     const void* new_value, int64_t value_stride_b, int64_t value_stride_h,
+                                     int32_t layer, psb_stream_t stream) {
+  if (a == nullptr || (new_key == nullptr) != (new_value == nullptr)) return PSB_ERR_INVALID;
+  return paged_decode_impl(query, q_stride_b, q_stride_h, out, o_stride_b, o_stride_h, a->k_cache, a->v_cache,
+                           new_key, key_stride_b, key_stride_h, new_value, value_stride_b, value_stride_h,
+                           a->block_tables, a->table_stride, a->context_lens, a->batch, a->q_heads, layer,
+                           a->num_layers, a->num_blocks, a->num_kv_heads, a->block_size, a->head_dim, a->dtype,
+                           a->max_context, a->scale, a->workspace, a->workspace_bytes, a->error_flag, stream);
+}
+
 extern "C" int psb_paged_decode_append(const void* query, int64_t q_stride_b, int64_t q_stride_h, void* out,
                                        int64_t o_stride_b, int64_t o_stride_h, void* k_cache, void* v_cache,
                                        const void* new_key, int64_t key_stride_b, int64_t key_stride_h,

@@ -19,6 +19,7 @@ returns without synchronising.  There is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
 import functools
 import math
 import threading
@@ -276,16 +277,17 @@ class DecodeLaunch:
     """The launch arguments of one decode batch that stay the same for all
     the layer calls of an iteration (pools, device table and lengths,
     geometry, workspace), kept by the reference-facing wrappers next to the
-    batch's metadata so a repeat layer call only adds the query, output, new
-    rows, layer and stream before one C call.
+    batch's metadata as one ``psb_decode_args`` struct, so a repeat layer call
+    passes only the query, output, new rows, layer and stream
+    (``psb_paged_decode_args``).
 
     Built from arguments the wrappers have already checked: pools contiguous
     and of the query's dtype, device table ``[B, M]`` int32 with unit inner
-    stride and contiguous int32 lengths.  The workspace it sized is held
-    here, so a later growth of the per-device workspace never leaves this
-    launch pointing at freed memory."""
+    stride and contiguous int32 lengths.  The workspace it sized, and the
+    table and lengths, are held here, so a later growth of the per-device
+    workspace never leaves this launch pointing at freed memory."""
 
-    __slots__ = ("lib", "k_ptr", "v_ptr", "batch", "q_heads", "dtype", "dev", "ws", "table_args", "tail")
+    __slots__ = ("lib", "k_ptr", "v_ptr", "batch", "q_heads", "dtype", "dev", "ws", "keep", "args", "args_ptr")
 
     def __init__(self, k_cache: torch.Tensor, v_cache: torch.Tensor, tables: torch.Tensor, lengths: torch.Tensor,
                  batch: int, q_heads: int, max_context: int, dtype: torch.dtype):
@@ -298,9 +300,14 @@ class DecodeLaunch:
         self.dev = k_cache.device.index if k_cache.device.index is not None else torch.cuda.current_device()
         need = decode_workspace_bytes(self.batch, self.q_heads, hkv, d, bs, int(max_context), dtype)
         self.ws = DecodeWorkspace.for_device(k_cache.device).get(need, self.batch, hkv)
-        self.table_args = (tables.data_ptr(), tables.stride(0), lengths.data_ptr(), self.batch, self.q_heads)
-        self.tail = (nl, nb, hkv, bs, d, _DTYPES[dtype], int(max_context), 1.0 / math.sqrt(d), self.ws.data_ptr(),
-                     self.ws.numel() * self.ws.element_size(), None)
+        self.keep = (tables, lengths)
+        self.args = _native.DecodeArgs(
+            k_cache=self.k_ptr, v_cache=self.v_ptr, block_tables=tables.data_ptr(), table_stride=tables.stride(0),
+            context_lens=lengths.data_ptr(), num_blocks=nb, workspace=self.ws.data_ptr(),
+            workspace_bytes=self.ws.numel() * self.ws.element_size(), error_flag=None, batch=self.batch,
+            q_heads=self.q_heads, num_layers=nl, num_kv_heads=hkv, block_size=bs, head_dim=d,
+            dtype=_DTYPES[dtype], max_context=int(max_context), scale=1.0 / math.sqrt(d), reserved=0)
+        self.args_ptr = ctypes.addressof(self.args)
 
     def matches(self, k_cache: torch.Tensor, v_cache: torch.Tensor, query: torch.Tensor) -> bool:
         return (k_cache.data_ptr() == self.k_ptr and v_cache.data_ptr() == self.v_ptr
@@ -314,20 +321,19 @@ class DecodeLaunch:
             query = query.contiguous()
         out = torch.empty_like(query)
         stream = _raw_stream(self.dev) if _raw_stream is not None else torch.cuda.current_stream(self.dev).cuda_stream
-        head = (query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
-                self.k_ptr, self.v_ptr)
         if new_key is None:
-            _native.check(self.lib.psb_paged_decode(*head, *self.table_args, layer, *self.tail, stream),
-                          "paged_decode")
+            _native.check(self.lib.psb_paged_decode_args(
+                self.args_ptr, query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0),
+                out.stride(1), None, 0, 0, None, 0, 0, layer, stream), "paged_decode")
             return out
         if new_key.stride(-1) != 1:
             new_key = new_key.contiguous()
         if new_value.stride(-1) != 1:
             new_value = new_value.contiguous()
-        _native.check(self.lib.psb_paged_decode_append(
-            *head, new_key.data_ptr(), new_key.stride(0), new_key.stride(1), new_value.data_ptr(),
-            new_value.stride(0), new_value.stride(1), *self.table_args, layer, *self.tail, stream),
-            "paged_decode_append")
+        _native.check(self.lib.psb_paged_decode_args(
+            self.args_ptr, query.data_ptr(), query.stride(0), query.stride(1), out.data_ptr(), out.stride(0),
+            out.stride(1), new_key.data_ptr(), new_key.stride(0), new_key.stride(1), new_value.data_ptr(),
+            new_value.stride(0), new_value.stride(1), layer, stream), "paged_decode_append")
         return out
 
 

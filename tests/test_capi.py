@@ -132,3 +132,23 @@ def test_static_decode_checks_need_no_gpu():
     # bad geometry (q heads not a multiple of kv heads)
     assert lib.psb_paged_decode_static(fake, 0, 0, fake, 0, 0, fake, fake, fake, 8, fake, 4, 14, 0, 1, 8, 3, 16, 64,
                                        _native.PSB_BF16, 128, 0.125, null, null) == _native.PSB_ERR_INVALID
+
+
+def test_decode_args_struct_and_checks():
+    """psb_decode_args has the binding's layout, and psb_paged_decode_args
+    rejects a null struct, one null new row pointer, and the null pointers
+    psb_paged_decode rejects, before any CUDA call."""
+    lib = _native.load()
+    assert lib.psb_decode_args_size() == ctypes.sizeof(_native.DecodeArgs)
+    offsets = {name: getattr(_native.DecodeArgs, name).offset for name, _ in _native.DecodeArgs._fields_}
+    assert offsets["k_cache"] == 0 and offsets["batch"] == 72 and offsets["scale"] == 104
+    null = None
+    assert lib.psb_paged_decode_args(null, null, 0, 0, null, 0, 0, null, 0, 0, null, 0, 0, 0,
+                                     null) == _native.PSB_ERR_INVALID
+    a = _native.DecodeArgs(batch=1, q_heads=14, num_layers=1, num_blocks=8, num_kv_heads=2, block_size=16,
+                           head_dim=64, dtype=_native.PSB_BF16, max_context=16, table_stride=1, scale=0.125)
+    ap = ctypes.addressof(a)
+    assert lib.psb_paged_decode_args(ap, null, 0, 0, null, 0, 0, null, 0, 0, null, 0, 0, 0,
+                                     null) == _native.PSB_ERR_INVALID  # null query / pools / table
+    assert lib.psb_paged_decode_args(ap, 16, 64, 64, 16, 64, 64, 16, 0, 0, null, 0, 0, 0,
+                                     null) == _native.PSB_ERR_INVALID  # new_key without new_value

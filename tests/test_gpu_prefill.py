@@ -135,3 +135,28 @@ def test_varlen_longest_prompt():
     assert mx <= 2e-2 and mean <= 2e-3, (mx, mean)
     mx, _ = err_stats(out[b - 128:b], exact[b - 128:b])
     assert mx <= 2e-2
+
+
+@pytest.mark.parametrize("pad", [2, 64])
+def test_varlen_strided_output(pad):
+    """Output rows in a wider buffer [T, Hq, 64 + pad]: pad 2 makes the head
+    stride 132 bytes (the per-thread store path of the tensor-core epilogue),
+    pad 64 keeps 16-byte rows (the path through the per-warp staging area);
+    the padding columns must stay untouched."""
+    from pagedserve_b200 import ops
+    lens = [200, 1, 130, 64, 383]
+    c = varlen_case(13, lens, dtype="bfloat16")
+    q, k, v = (to_dev(c[x], "bfloat16") for x in ("q", "k", "v"))
+    t, hq, d = q.shape
+    wide = torch.full((t, hq, d + pad), 7.0, dtype=torch.bfloat16, device="cuda")
+    out = wide[:, :, :d]
+    cu = torch.from_numpy(np.asarray(c["cu_seqlens"], dtype=np.int32)).cuda()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    res = ops.varlen_prefill(q, k, v, cu, max(lens), out=out, error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and res.data_ptr() == out.data_ptr()
+    assert bool((wide[:, :, d:] == 7.0).all())
+    exact = ora.varlen_causal_attention(c["q"], c["k"], c["v"], c["cu_seqlens"])
+    mx, mean = err_stats(out, exact)
+    max_tol, mean_tol = TOL["bfloat16"]
+    assert mx <= max_tol and mean <= mean_tol, (mx, mean)
