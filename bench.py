@@ -886,27 +886,31 @@ def run_b200(args, world, rank, local):
 
     # ---- end to end through the reference-facing API, host buffers -------
     # Every step copies its inputs (q, new k, new v: one pinned staging
-    # buffer) to the device and its output back to pinned host memory.  One
-    # copy stream carries, per step s, the read-back of step s - 1's output
-    # and the upload of step s + 1's inputs (two alternating device input
-    # buffers), so both overlap step s's kernel, as a serving loop pipelines
-    # them; one event orders each direction.
+    # buffer) to the device and its output back to pinned host memory.  Per
+    # step s, an upload stream copies step s + 1's inputs and a read-back
+    # stream step s - 1's output, both overlapping step s's kernel and each
+    # other (PCIe carries both directions at once), as a serving loop
+    # pipelines them.  Each step of a run has its own device input buffer and
+    # its output is kept until the run ends, so no copy ever waits for a
+    # buffer to be free and no memory is reused while a copy reads it.
     cache, ids, positions = w["cache"], w["ids"], w["positions"]
     q_bytes, kv_bytes = w["q"].numel() * 2, w["new_k"].numel() * 2
     in_host = torch.empty(q_bytes + 2 * kv_bytes, dtype=torch.uint8).pin_memory()
     in_host[:q_bytes].view(torch.bfloat16).copy_(w["q"].reshape(-1).cpu())
     in_host[q_bytes:q_bytes + kv_bytes].view(torch.bfloat16).copy_(w["new_k"].reshape(-1).cpu())
     in_host[q_bytes + kv_bytes:].view(torch.bfloat16).copy_(w["new_v"].reshape(-1).cpu())
-    in_dev = [torch.empty_like(in_host, device=device) for _ in range(2)]
+    e2e_steps = 2 * LAYERS  # timed: two whole decode iterations
+    n_buf = e2e_steps + 1
+    in_dev = [torch.empty_like(in_host, device=device) for _ in range(n_buf)]
     views = [(buf[:q_bytes].view(torch.bfloat16).view(batch, HQ, 1, D),
               buf[q_bytes:q_bytes + kv_bytes].view(torch.bfloat16).view(batch, HKV, D),
               buf[q_bytes + kv_bytes:].view(torch.bfloat16).view(batch, HKV, D)) for buf in in_dev]
     o_host = [torch.empty((batch, HQ, 1, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    s_copy = torch.cuda.Stream(device)
+    s_up, s_down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
-    o_keep = [None, None]
-    # The copies and the two events go straight to the CUDA runtime on
-    # explicit streams (cuda-python): the same operations as torch's
+    outs = [None] * n_buf
+    # The copies and the events go straight to the CUDA runtime on explicit
+    # streams (cuda-python): the same operations as torch's
     # copy_/Event/wait_event, at a fraction of their host cost in this
     # host-bound loop.
     from cuda.bindings import runtime as cudart
@@ -918,22 +922,24 @@ def run_b200(args, world, rank, local):
             raise RuntimeError(f"CUDA runtime call failed: {res[0]}")
         return res[1] if len(res) > 1 else None
 
-    copy_h, comp_h = s_copy.cuda_stream, compute.cuda_stream
-    ev_in = [rt_check(cudart.cudaEventCreateWithFlags(cudart.cudaEventDisableTiming)) for _ in range(2)]
-    ev_done = [rt_check(cudart.cudaEventCreateWithFlags(cudart.cudaEventDisableTiming)) for _ in range(2)]
+    def rt_events():
+        return [rt_check(cudart.cudaEventCreateWithFlags(cudart.cudaEventDisableTiming)) for _ in range(2)]
+
+    up_h, down_h, comp_h = s_up.cuda_stream, s_down.cuda_stream, compute.cuda_stream
+    ev_in, ev_done = rt_events(), rt_events()  # step s's upload / kernel done (slot s % 2)
     in_ptr, in_dev_ptr = in_host.data_ptr(), [b.data_ptr() for b in in_dev]
     in_n, o_n = in_host.numel(), o_host[0].numel() * 2
     o_host_ptr = [t.data_ptr() for t in o_host]
 
     from pagedserve_b200.attention import clear_metadata_cache
 
-    def upload(s):  # step s's inputs into buffer s % 2 (its last reader, step s - 2, is done)
-        rt_check(cudart.cudaMemcpyAsync(in_dev_ptr[s % 2], in_ptr, in_n, k_h2d, copy_h))
-        rt_check(cudart.cudaEventRecord(ev_in[s % 2], copy_h))
+    def upload(s):  # step s's inputs into its own buffer
+        rt_check(cudart.cudaMemcpyAsync(in_dev_ptr[s], in_ptr, in_n, k_h2d, up_h))
+        rt_check(cudart.cudaEventRecord(ev_in[s % 2], up_h))
 
     def read_back(s):  # step s's output, once its kernel is done
-        rt_check(cudart.cudaStreamWaitEvent(copy_h, ev_done[s % 2], 0))
-        rt_check(cudart.cudaMemcpyAsync(o_host_ptr[s % 2], o_keep[s % 2].data_ptr(), o_n, k_d2h, copy_h))
+        rt_check(cudart.cudaStreamWaitEvent(down_h, ev_done[s % 2], 0))
+        rt_check(cudart.cudaMemcpyAsync(o_host_ptr[s % 2], outs[s].data_ptr(), o_n, k_d2h, down_h))
 
     # Each decode iteration passes new positions, as a serving loop does: here
     # iteration k decodes at positions ctx - 1 - k (inside each request's
@@ -944,42 +950,43 @@ def run_b200(args, world, rank, local):
     host_us = [0.0, 0.0]  # host time in the API call: first layer call of an iteration, the others
 
     def e2e_step(s, first_iteration):
-        i, layer = s % 2, s % LAYERS
+        layer = s % LAYERS
         pos = iter_positions[first_iteration + s // LAYERS]
         if s >= 1:
-            read_back(s - 1)  # also orders the upload below after step s - 1's kernel
+            read_back(s - 1)
         upload(s + 1)
-        rt_check(cudart.cudaStreamWaitEvent(comp_h, ev_in[i], 0))
-        # step s - 2's output: its read-back precedes ev_in[i] on the copy stream
-        o_keep[i] = None
-        qd, kd, vd = views[i]
+        rt_check(cudart.cudaStreamWaitEvent(comp_h, ev_in[s % 2], 0))
+        qd, kd, vd = views[s]
         h0 = time.perf_counter()
-        o_keep[i] = paged_decode_attention_with_write(qd, kd, vd, cache, ids, pos, layer)
+        outs[s] = paged_decode_attention_with_write(qd, kd, vd, cache, ids, pos, layer)
         host_us[0 if layer == 0 else 1] += 1e6 * (time.perf_counter() - h0)
-        rt_check(cudart.cudaEventRecord(ev_done[i], comp_h))
+        rt_check(cudart.cudaEventRecord(ev_done[s % 2], comp_h))
 
     def e2e_run(n, first_iteration):
-        s_copy.wait_stream(compute)
+        s_up.wait_stream(compute)
+        s_down.wait_stream(compute)
         upload(0)
         for s in range(n):
             e2e_step(s, first_iteration)
         read_back(n - 1)
-        compute.wait_stream(s_copy)
+        compute.wait_stream(s_up)
+        compute.wait_stream(s_down)
 
-    # one whole decode iteration of warm-up (pinned staging and the metadata
-    # path warm), then whole iterations timed: every iteration's first layer
-    # call rebuilds and copies the block tables, as a new iteration would
-    e2e_steps = 2 * LAYERS
+    # as many warm-up steps as timed ones (pinned staging, the metadata path
+    # and the allocator's cached blocks for the outputs all warm), then whole
+    # iterations timed: every iteration's first layer call rebuilds and copies
+    # the lengths, as a new iteration would
     clear_metadata_cache(cache)
-    e2e_run(LAYERS, 0)
+    e2e_run(e2e_steps, 0)
     torch.cuda.synchronize()
+    outs[:] = [None] * n_buf  # back to the allocator, which hands them to the timed steps
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     host_us[:] = [0.0, 0.0]
     h_start = time.perf_counter()
     e_start.record(compute)
-    e2e_run(e2e_steps, 1)
+    e2e_run(e2e_steps, e2e_steps // LAYERS)
     e_end.record(compute)
     host_loop_us = 1e6 * (time.perf_counter() - h_start) / e2e_steps
     torch.cuda.synchronize()
@@ -987,6 +994,7 @@ def run_b200(args, world, rank, local):
     e2e_ms = e_start.elapsed_time(e_end) / e2e_steps
     for ev in ev_in + ev_done:
         rt_check(cudart.cudaEventDestroy(ev))
+    outs[:] = [None] * n_buf
     iterations = e2e_steps // LAYERS  # lengths copies inside the timed region
     h2d = in_host.numel() + 4 * batch * iterations / e2e_steps
     # iteration k attends over ctx - k tokens per request
@@ -1005,7 +1013,7 @@ def run_b200(args, world, rank, local):
     step_ms, dec_ms, e2e_ms, single_ms, two_ms = (max(r[k] for r in per_rank) for k in
                                                  ("step_ms", "dec_ms", "e2e_ms", "single_ms", "two_ms"))
     total_bytes, total_seqs = sum(r["bytes"] for r in per_rank), int(sum(r["seqs"] for r in per_rank))
-    del w, graphs, g_single, in_dev, o_keep
+    del w, graphs, g_single, in_dev, views, outs
     torch.cuda.empty_cache()
 
     # ---- the other sections (each rank on its own GPU) ----------------------
@@ -1058,12 +1066,12 @@ def run_b200(args, world, rank, local):
                                     "other_calls": round(host_us[1] / (e2e_steps - e2e_steps // LAYERS), 1)},
                     "path": "per layer call: q, new k, new v copied from one pinned host staging buffer, "
                             "paged_decode_attention_with_write (reference-facing API: write_token + decode in "
-                            "one launch), output copied back to pinned host memory; the read-back of step s - 1 "
-                            "and the upload of step s + 1 (two alternating device input buffers, cudaMemcpyAsync) "
-                            "on one copy stream, overlapping step s's kernel; each iteration's first layer call "
-                            "rebuilds and "
+                            "one launch), output copied back to pinned host memory; the upload of step s + 1 "
+                            "(a device input buffer per step, outputs kept until the run ends) and the read-back "
+                            "of step s - 1 on two copy streams (cudaMemcpyAsync), overlapping step s's kernel and "
+                            "each other; each iteration's first layer call rebuilds and "
                             "copies the lengths for its new positions (the block table stays on the device within "
-                            f"a cache epoch); timed over 2 whole iterations ({LAYERS} layer calls each) after one "
+                            f"a cache epoch); timed over 2 whole iterations ({LAYERS} layer calls each) after two "
                             "of warm-up"},
             "gpu_launches": 2 * args.steps,
             "gpu_launches_note": "per step: decode (with the new-token store), combine",
