@@ -110,6 +110,7 @@ def clear_metadata_cache(cache) -> None:
         last.clear()
     if getattr(cache, "_psb_table", None) is not None:
         cache._psb_table = None
+    cache._psb_fast = None
 
 
 def _host_metadata(cache, request_ids, positions, device):
@@ -245,8 +246,36 @@ def paged_decode_attention(query: torch.Tensor, cache, request_ids: Sequence[str
 
     Drop-in for ``triton_paged_decode_attention`` (triton_paged_decode.py:98-104).
     """
+    sig = (query.shape, query.dtype, query.get_device())
+    meta = _repeat(cache, sig, request_ids, positions, layer)
+    if meta is not None:
+        return meta.launch(query, layer)
     meta = _validated_metadata(query, cache, request_ids, positions, layer)
-    return _launch(meta, cache, query, layer)
+    out = _launch(meta, cache, query, layer)
+    _remember(cache, sig, meta)
+    return out
+
+
+# The layer calls of one decode iteration repeat the same lists and tensors of
+# the same shapes, dtypes and devices.  After a call passed every check, the
+# cache keeps (signature of its tensors, its metadata, device, layers, pools);
+# a later call whose signature is equal and whose lists hit that same
+# metadata has passed the same checks, all but the layer index, which is
+# checked here.  Anything else takes the full path and its error messages.
+def _repeat(cache, sig, request_ids, positions, layer):
+    fast = getattr(cache, "_psb_fast", None)
+    if fast is None or fast[0] != sig or not 0 <= layer < fast[3]:
+        return None
+    kv = cache.kv_cache
+    if kv.k_cache is not fast[4] or kv.v_cache is not fast[5]:
+        return None
+    meta = _last_hit(cache, "table", request_ids, positions, fast[2])
+    return meta if meta is fast[1] and meta.launch is not None else None
+
+
+def _remember(cache, sig, meta) -> None:
+    kv = cache.kv_cache
+    cache._psb_fast = (sig, meta, sig[2], kv.k_cache.shape[0], kv.k_cache, kv.v_cache)
 
 
 def _launch(meta: "_Meta", cache, query, layer, new_key=None, new_value=None):
@@ -313,6 +342,11 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     ``[B, Hkv, 1, D]``) and row b lands at ``positions[b]``, the last position
     the query attends to.  Runs as ``psb_paged_decode_append``.
     """
+    sig = (query.shape, query.dtype, query.get_device(), key.shape, key.dtype, key.get_device(), value.shape,
+           value.dtype, value.get_device())
+    meta = _repeat(cache, sig, request_ids, positions, layer)
+    if meta is not None:
+        return meta.launch(query, layer, key, value)
     if not query.is_cuda:
         raise ValueError(_CUDA_REQUIRED)
     kv = cache.kv_cache
@@ -329,7 +363,9 @@ def paged_decode_attention_with_write(query: torch.Tensor, key: torch.Tensor, va
     dev = query.get_device()
     if key.get_device() != dev or value.get_device() != dev:
         raise ValueError("new K/V must be on the query's device")
-    return _launch(meta, cache, query, layer, key, value)
+    out = _launch(meta, cache, query, layer, key, value)
+    _remember(cache, sig, meta)
+    return out
 
 
 def _rows_shape(t: torch.Tensor) -> tuple:

@@ -155,3 +155,49 @@ def test_reference_facing_write_and_attend():
     assert torch.equal(caches[0].kv_cache.v_cache, caches[1].kv_cache.v_cache)
     with pytest.raises(ValueError, match="Expected K/V shape"):
         paged_decode_attention_with_write(q, nk[:, :1], nv[:, :1], caches[1], ids, pos, 1)
+
+
+def test_repeat_calls_keep_every_check():
+    """Layer calls that repeat the last call's lists and tensor signature skip
+    the re-validation; the result is the full path's, and a call that differs
+    in anything the reference wrapper checks still raises its error."""
+    from pagedserve_b200 import PagedKVCache, paged_decode_attention, paged_decode_attention_with_write
+    from pagedserve_b200.attention import clear_metadata_cache
+    lens = [5, 40, 17]
+    cache = PagedKVCache(num_blocks=32, num_layers=3, num_kv_heads=2, head_dim=64, block_size=16,
+                         dtype=torch.bfloat16, device="cuda", free_order=np.random.default_rng(4).permutation(32))
+    ids = [f"r{i}" for i in range(len(lens))]
+    for rid, n in zip(ids, lens):
+        cache.allocate(rid, n)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    cache.kv_cache.k_cache.copy_(torch.randn(cache.kv_cache.k_cache.shape, generator=g, device="cuda"))
+    cache.kv_cache.v_cache.copy_(torch.randn(cache.kv_cache.v_cache.shape, generator=g, device="cuda"))
+    pos = [n - 1 for n in lens]
+    q = torch.randn(len(lens), 14, 1, 64, generator=g, device="cuda").to(torch.bfloat16)
+    nk = torch.randn(len(lens), 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    nv = torch.randn(len(lens), 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    first = [paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, layer) for layer in range(3)]
+    again = [paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, layer) for layer in range(3)]
+    plain = paged_decode_attention(q, cache, ids, pos, 2)
+    clear_metadata_cache(cache)
+    full = paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, 2)
+    torch.cuda.synchronize()
+    for a, b in zip(first, again):
+        assert torch.equal(a, b)
+    assert torch.equal(full, again[2]) and torch.equal(plain, again[2])
+    with pytest.raises(ValueError, match="Invalid layer"):
+        paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, 3)
+    with pytest.raises(ValueError, match="Invalid layer"):
+        paged_decode_attention(q, cache, ids, pos, -1)
+    with pytest.raises(ValueError, match="Invalid position"):
+        paged_decode_attention_with_write(q, nk, nv, cache, ids, [pos[0], pos[1] + 1, pos[2]], 0)
+    with pytest.raises(ValueError, match="unique"):
+        paged_decode_attention_with_write(q, nk, nv, cache, [ids[0], ids[0], ids[2]], pos, 0)
+    with pytest.raises(ValueError, match="dtype"):
+        paged_decode_attention_with_write(q.float(), nk, nv, cache, ids, pos, 0)
+    with pytest.raises(ValueError, match="Expected K/V shape"):
+        paged_decode_attention_with_write(q, nk[:, :1], nv[:, :1], cache, ids, pos, 0)
+    # after the errors, the repeat path still returns the full path's result
+    again2 = paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(again2, full)
