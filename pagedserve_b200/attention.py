@@ -145,15 +145,16 @@ def _build_metadata(cache, request_ids, positions, device):
             dev = host.to(device, non_blocking=True)
             done()
             tables = dev[: b * width].view(b, width)
-            cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts)
-            return _Meta(tables, dev[b * width:], width)
-        tables, width, rows, counts = table
+            holder = [None]  # the launch struct of the first call over this table, a template for the next
+            cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts, holder)
+            return _Meta(tables, dev[b * width:], width, holder)
+        tables, width, rows, counts, holder = table
         _check_positions(pos, counts, positions, request_ids)
         host, done = _staging(cache, b, device)
         host.numpy()[:] = pos + 1
         dev = host.to(device, non_blocking=True)
         done()
-        return _Meta(tables, dev, width)
+        return _Meta(tables, dev, width, holder)
     else:
         # any cache with the reference's interface
         lengths = np.empty(len(request_ids), dtype=np.int32)
@@ -187,31 +188,41 @@ def _staging(cache, n: int, device):
         return torch.empty(n, dtype=torch.int32), (lambda: None)
     ring = getattr(cache, "_psb_staging", None)
     if ring is None:
-        ring = cache._psb_staging = [[None, None], [None, None], 0]  # [buffer, event] x 2, next slot
+        # [buffer, event, event recorded] x 2, next slot; an event per slot, made once
+        ring = cache._psb_staging = [[None, torch.cuda.Event(), False], [None, torch.cuda.Event(), False], 0]
     slot = ring[2]
     ring[2] = 1 - slot
-    buf, ev = ring[slot]
-    if ev is not None:
+    entry = ring[slot]
+    buf, ev = entry[0], entry[1]
+    if entry[2]:
         ev.synchronize()  # normally long complete: the slot was used an iteration ago
     if buf is None or buf.numel() < n:
         buf = torch.empty(max(n, 2 * (buf.numel() if buf is not None else 0)), dtype=torch.int32, pin_memory=True)
-        ring[slot][0] = buf
+        entry[0] = buf
 
     def done():
-        e = torch.cuda.Event()
-        e.record(torch.cuda.current_stream(device))
-        ring[slot][1] = e
+        ev.record(torch.cuda.current_stream(device))
+        entry[2] = True
 
     return buf[:n], done
 
 
 def _table_for(cache, request_ids, device):
-    """(tables, width, store rows, token counts) built earlier in this epoch
-    for this request list on this device, or None."""
+    """(tables, width, store rows, token counts, launch template holder)
+    built earlier in this epoch for this request list on this device, or None."""
     kept = getattr(cache, "_psb_table", None)
     if kept is None or kept[0] != cache.metadata_epoch or kept[1] != device or kept[2] != request_ids:
         return None
     return kept[3:]
+
+
+def _unique_known(cache, request_ids) -> bool:
+    """True when ``request_ids`` is the list the table kept for this epoch
+    was built for (a table is built only after the ids passed the uniqueness
+    check)."""
+    kept = getattr(cache, "_psb_table", None)
+    return (kept is not None and kept[0] == getattr(cache, "metadata_epoch", None) and type(request_ids) is list
+            and kept[2] == request_ids)
 
 
 def _check_positions(pos: np.ndarray, counts: np.ndarray, positions, request_ids) -> None:
@@ -227,11 +238,12 @@ class _Meta:
     that stay the same for all layer calls over them (``ops.DecodeLaunch``,
     built on the first call)."""
 
-    __slots__ = ("tables", "lengths", "width", "launch")
+    __slots__ = ("tables", "lengths", "width", "launch", "holder")
 
-    def __init__(self, tables, lengths, width):
+    def __init__(self, tables, lengths, width, holder=None):
         self.tables, self.lengths, self.width = tables, lengths, width
         self.launch = None
+        self.holder = holder  # a one-element list shared by the metadata built over the same device table
 
     def __iter__(self):  # (tables, lengths, width)
         return iter((self.tables, self.lengths, self.width))
@@ -282,9 +294,16 @@ def _launch(meta: "_Meta", cache, query, layer, new_key=None, new_value=None):
     kv = cache.kv_cache
     launch = meta.launch
     if launch is None or not launch.matches(kv.k_cache, kv.v_cache, query):
-        launch = meta.launch = ops.DecodeLaunch(kv.k_cache, kv.v_cache, meta.tables, meta.lengths,
-                                                query.shape[0], query.shape[1], meta.width * cache.block_size,
-                                                query.dtype)
+        tmpl = meta.holder[0] if meta.holder is not None else None
+        if tmpl is not None and tmpl.matches(kv.k_cache, kv.v_cache, query):
+            # the same device table: only the lengths differ
+            launch = meta.launch = tmpl.with_lengths(meta.lengths)
+        else:
+            launch = meta.launch = ops.DecodeLaunch(kv.k_cache, kv.v_cache, meta.tables, meta.lengths,
+                                                    query.shape[0], query.shape[1], meta.width * cache.block_size,
+                                                    query.dtype)
+            if meta.holder is not None:
+                meta.holder[0] = launch
     return launch(query, layer, new_key, new_value)
 
 
@@ -311,7 +330,7 @@ def _validated_metadata(query, cache, request_ids, positions, layer):
     # the metadata of an earlier call with these very lists was built only
     # after they passed every check here, uniqueness included
     meta = _last_hit(cache, "table", request_ids, positions, dev)
-    if meta is None and len(set(request_ids)) != batch:
+    if meta is None and not _unique_known(cache, request_ids) and len(set(request_ids)) != batch:
         raise ValueError("Request IDs must be unique")
     if head_dim != kv.head_dim:
         raise ValueError("Head dimension mismatch")

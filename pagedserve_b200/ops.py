@@ -309,6 +309,18 @@ class DecodeLaunch:
             dtype=_DTYPES[dtype], max_context=int(max_context), scale=1.0 / math.sqrt(d), reserved=0)
         self.args_ptr = ctypes.addressof(self.args)
 
+    def with_lengths(self, lengths: torch.Tensor) -> "DecodeLaunch":
+        """The same launch over another lengths array (contiguous int32 [B]
+        on the same device) with the same table and bound."""
+        new = object.__new__(DecodeLaunch)
+        for name in ("lib", "k_ptr", "v_ptr", "batch", "q_heads", "dtype", "dev", "ws"):
+            setattr(new, name, getattr(self, name))
+        new.keep = (self.keep[0], lengths)
+        new.args = _native.DecodeArgs.from_buffer_copy(self.args)
+        new.args.context_lens = lengths.data_ptr()
+        new.args_ptr = ctypes.addressof(new.args)
+        return new
+
     def matches(self, k_cache: torch.Tensor, v_cache: torch.Tensor, query: torch.Tensor) -> bool:
         return (k_cache.data_ptr() == self.k_ptr and v_cache.data_ptr() == self.v_ptr
                 and query.shape[0] == self.batch and query.shape[1] == self.q_heads and query.dtype == self.dtype)
