@@ -28,7 +28,7 @@ constexpr int kMaxDevices = 64;
 // in every call, so it needs no clearing), on the CUDA-core path the
 // per-(sequence, kv head) arrival counters, which that path zeroes itself at
 // the start of every call, and the per-chunk partials.
-__device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
 
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
