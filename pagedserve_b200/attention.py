@@ -127,34 +127,32 @@ def _build_metadata(cache, request_ids, positions, device):
         # this package's PagedKVCache: vectorised over its table store, the
         # table gathered straight into pinned memory as [table (B x W) | lengths (B)]
         b = len(request_ids)
-        pos = np.fromiter(positions, dtype=np.int64, count=b)
         table = _table_for(cache, request_ids, device)
-        if table is None:
-            # the batch's device table, kept per (epoch, request list): within
-            # an epoch the blocks do not change (the scheduler reserves a
-            # request's whole capacity when it admits it), so the decode
-            # iterations that follow rebuild only the lengths
-            rows = cache.table_store_rows(request_ids)
-            counts = cache.store_token_counts(rows)
-            _check_positions(pos, counts, positions, request_ids)
-            width = cache.table_width(rows)
-            host, done = _staging(cache, b * (width + 1), device)
-            flat = host.numpy()
-            cache.gather_tables(rows, flat, width)
-            flat[b * width:] = pos + 1
-            dev = host.to(device, non_blocking=True)
-            done()
-            tables = dev[: b * width].view(b, width)
-            holder = [None]  # the launch struct of the first call over this table, a template for the next
-            cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts, holder)
-            return _Meta(tables, dev[b * width:], width, holder)
-        tables, width, rows, counts, holder = table
+        if table is not None:
+            tables, width, rows, counts, holder = table
+            return _Meta(tables, _upload_lengths(cache, holder, positions, counts, request_ids, device), width,
+                         holder)
+        # the batch's device table, kept per (epoch, request list): within an
+        # epoch the blocks do not change (the scheduler reserves a request's
+        # whole capacity when it admits it), so the decode iterations that
+        # follow upload only the lengths
+        pos = np.fromiter(positions, dtype=np.int64, count=b)
+        rows = cache.table_store_rows(request_ids)
+        counts = cache.store_token_counts(rows)
         _check_positions(pos, counts, positions, request_ids)
-        host, done = _staging(cache, b, device)
-        host.numpy()[:] = pos + 1
+        width = cache.table_width(rows)
+        host, done = _staging(cache, b * (width + 1), device)
+        flat = host.numpy()
+        cache.gather_tables(rows, flat, width)
+        flat[b * width:] = pos + 1
         dev = host.to(device, non_blocking=True)
         done()
-        return _Meta(tables, dev, width, holder)
+        tables = dev[: b * width].view(b, width)
+        # [launch struct of the first call over this table (a template for
+        # the next), lengths ring (added by the first new-positions upload)]
+        holder = [None]
+        cache._psb_table = (cache.metadata_epoch, device, list(request_ids), tables, width, rows, counts, holder)
+        return _Meta(tables, dev[b * width:], width, holder)
     else:
         # any cache with the reference's interface
         lengths = np.empty(len(request_ids), dtype=np.int32)
@@ -214,6 +212,56 @@ def _table_for(cache, request_ids, device):
     if kept is None or kept[0] != cache.metadata_epoch or kept[1] != device or kept[2] != request_ids:
         return None
     return kept[3:]
+
+
+_LEN_SLOTS = _KEEP + 3  # lengths arrays per device table in turn (more than the metadata entries kept)
+
+
+def _upload_lengths(cache, holder, positions, counts, request_ids, device):
+    """The device lengths (``positions[b] + 1``, int32) of a new decode
+    iteration over a device table kept for this epoch, after the reference's
+    position check.
+
+    Each table keeps a ring of ``_LEN_SLOTS`` pinned host rows and device
+    rows: the positions are written straight into the next host row, checked
+    with one unsigned comparison against the token counts (a negative position
+    wraps above every count), turned into lengths in place and copied to the
+    next device row on the current stream.  A host row is refilled only after
+    its previous copy has completed (an event per row); a device row is
+    rewritten only after more iterations than the metadata entries kept, by
+    copies ordered after every launch that read it."""
+    b = len(request_ids)
+    if device.type != "cuda":  # host metadata (tests of the table logic): no ring
+        pos = np.fromiter(positions, dtype=np.int64, count=b)
+        _check_positions(pos, counts, positions, request_ids)
+        return torch.from_numpy((pos + 1).astype(np.int32))
+    ring = holder[1] if len(holder) > 1 else None
+    if ring is None:
+        host = torch.empty((_LEN_SLOTS, b), dtype=torch.int32, pin_memory=True)
+        ring = [host, host.numpy(), torch.empty((_LEN_SLOTS, b), dtype=torch.int32, device=device),
+                [torch.cuda.Event() for _ in range(_LEN_SLOTS)], [False] * _LEN_SLOTS, 0,
+                np.asarray(counts, dtype=np.int64).clip(0, 2 ** 31 - 1).astype(np.uint32)]
+        holder.append(ring)
+    host, host_np, dev, events, recorded, slot, counts_u32 = ring
+    ring[5] = (slot + 1) % _LEN_SLOTS
+    if recorded[slot]:
+        events[slot].synchronize()  # normally long complete: the row was used several iterations ago
+    row = host_np[slot]
+    try:
+        row[:] = positions
+    except (OverflowError, TypeError, ValueError):
+        row = None
+    if row is None or bool((row.view(np.uint32) >= counts_u32).any()):
+        for i, (rid, p) in enumerate(zip(request_ids, positions)):  # the first bad row, as the reference reports it
+            if not 0 <= p < int(counts[i]):
+                raise ValueError(f"Invalid position {p} for {rid}")
+        raise ValueError("Invalid positions")
+    row += 1
+    out = dev[slot]
+    out.copy_(host[slot], non_blocking=True)
+    events[slot].record(torch.cuda.current_stream(device))
+    recorded[slot] = True
+    return out
 
 
 def _unique_known(cache, request_ids) -> bool:
