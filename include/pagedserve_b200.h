@@ -397,6 +397,16 @@ int psb_add_rms_norm(const void* x, int64_t x_stride, void* residual, int64_t re
 int psb_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride, int32_t rows,
                      int32_t intermediate, int32_t dtype, psb_stream_t stream);
 
+/*
+ * bounded_wait_check: a self-test with no counterpart in the reference.  One
+ * warp waits, with the same bounded wait the library's kernels use, on a
+ * barrier that nothing completes; after the wall-clock bound (2 s) it gives
+ * up, ORs PSB_DEVERR_TIMEOUT (16) into *error_flag and returns.  A host uses
+ * it to see that a wait that cannot finish ends with a status on its stream
+ * rather than a hang, and that the device stays usable afterwards.
+ */
+int psb_bounded_wait_check(int32_t* error_flag, psb_stream_t stream);
+
 /* Number of SMs of the current device (for callers sizing persistent grids). */
 int psb_device_sm_count(void);
 

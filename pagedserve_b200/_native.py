@@ -49,6 +49,7 @@ SIGNATURES = {
     "psb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "psb_last_cuda_error": (ctypes.c_int, []),
     "psb_device_sm_count": (ctypes.c_int, []),
+    "psb_bounded_wait_check": (ctypes.c_int, [_c_void_p, _c_void_p]),
     "psb_reshape_and_cache": (ctypes.c_int, [
         _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i64,
         _i32, _i32, _i32, _i32, _c_void_p, _c_void_p]),

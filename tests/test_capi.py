@@ -152,3 +152,8 @@ def test_decode_args_struct_and_checks():
                                      null) == _native.PSB_ERR_INVALID  # null query / pools / table
     assert lib.psb_paged_decode_args(ap, 16, 64, 64, 16, 64, 64, 16, 0, 0, null, 0, 0, 0,
                                      null) == _native.PSB_ERR_INVALID  # new_key without new_value
+
+
+def test_bounded_wait_check_rejects_null_flag():
+    lib = _native.load()
+    assert lib.psb_bounded_wait_check(None, None) == _native.PSB_ERR_INVALID
