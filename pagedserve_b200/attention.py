@@ -214,7 +214,7 @@ def _table_for(cache, request_ids, device):
     return kept[3:]
 
 
-_LEN_SLOTS = _KEEP + 3  # lengths arrays per device table in turn (more than the metadata entries kept)
+_LEN_SLOTS = 4  # pinned lengths rows per device table, filled in turn
 
 
 def _upload_lengths(cache, holder, positions, counts, request_ids, device):
@@ -222,14 +222,13 @@ def _upload_lengths(cache, holder, positions, counts, request_ids, device):
     iteration over a device table kept for this epoch, after the reference's
     position check.
 
-    Each table keeps a ring of ``_LEN_SLOTS`` pinned host rows and device
-    rows: the positions are written straight into the next host row, checked
-    with one unsigned comparison against the token counts (a negative position
-    wraps above every count), turned into lengths in place and copied to the
-    next device row on the current stream.  A host row is refilled only after
-    its previous copy has completed (an event per row); a device row is
-    rewritten only after more iterations than the metadata entries kept, by
-    copies ordered after every launch that read it."""
+    Each table keeps a ring of ``_LEN_SLOTS`` pinned host rows: the positions
+    are written straight into the next row, checked with one unsigned
+    comparison against the token counts (a negative position wraps above
+    every count), turned into lengths in place and copied on the current
+    stream to a device array of their own (kept metadata may outlive any
+    number of later iterations).  A host row is refilled only after its
+    previous copy has completed (an event per row)."""
     b = len(request_ids)
     if device.type != "cuda":  # host metadata (tests of the table logic): no ring
         pos = np.fromiter(positions, dtype=np.int64, count=b)
@@ -238,11 +237,10 @@ def _upload_lengths(cache, holder, positions, counts, request_ids, device):
     ring = holder[1] if len(holder) > 1 else None
     if ring is None:
         host = torch.empty((_LEN_SLOTS, b), dtype=torch.int32, pin_memory=True)
-        ring = [host, host.numpy(), torch.empty((_LEN_SLOTS, b), dtype=torch.int32, device=device),
-                [torch.cuda.Event() for _ in range(_LEN_SLOTS)], [False] * _LEN_SLOTS, 0,
+        ring = [host, host.numpy(), None, [torch.cuda.Event() for _ in range(_LEN_SLOTS)], [False] * _LEN_SLOTS, 0,
                 np.asarray(counts, dtype=np.int64).clip(0, 2 ** 31 - 1).astype(np.uint32)]
         holder.append(ring)
-    host, host_np, dev, events, recorded, slot, counts_u32 = ring
+    host, host_np, _, events, recorded, slot, counts_u32 = ring
     ring[5] = (slot + 1) % _LEN_SLOTS
     if recorded[slot]:
         events[slot].synchronize()  # normally long complete: the row was used several iterations ago
@@ -257,7 +255,7 @@ def _upload_lengths(cache, holder, positions, counts, request_ids, device):
                 raise ValueError(f"Invalid position {p} for {rid}")
         raise ValueError("Invalid positions")
     row += 1
-    out = dev[slot]
+    out = torch.empty(b, dtype=torch.int32, device=device)
     out.copy_(host[slot], non_blocking=True)
     events[slot].record(torch.cuda.current_stream(device))
     recorded[slot] = True

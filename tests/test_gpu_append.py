@@ -201,3 +201,30 @@ def test_repeat_calls_keep_every_check():
     again2 = paged_decode_attention_with_write(q, nk, nv, cache, ids, pos, 2)
     torch.cuda.synchronize()
     assert torch.equal(again2, full)
+
+
+def test_kept_metadata_survives_many_new_iterations():
+    """A position list kept in the metadata store (hit between every new
+    iteration, so it never ages out) still decodes with its own lengths after
+    many more iterations over the same device table have uploaded theirs."""
+    from pagedserve_b200 import PagedKVCache, paged_decode_attention
+    from pagedserve_b200.attention import clear_metadata_cache
+    lens = [40, 61, 33]
+    cache = PagedKVCache(num_blocks=32, num_layers=1, num_kv_heads=2, head_dim=64, block_size=16,
+                         dtype=torch.bfloat16, device="cuda", free_order=np.random.default_rng(6).permutation(32))
+    ids = [f"r{i}" for i in range(len(lens))]
+    for rid, n in zip(ids, lens):
+        cache.allocate(rid, n)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    cache.kv_cache.k_cache.copy_(torch.randn(cache.kv_cache.k_cache.shape, generator=g, device="cuda"))
+    cache.kv_cache.v_cache.copy_(torch.randn(cache.kv_cache.v_cache.shape, generator=g, device="cuda"))
+    q = torch.randn(len(lens), 14, 1, 64, generator=g, device="cuda").to(torch.bfloat16)
+    kept = [n - 1 for n in lens]
+    first = paged_decode_attention(q, cache, ids, kept, 0)
+    for k in range(1, 12):
+        paged_decode_attention(q, cache, ids, [n - 1 - k for n in lens], 0)
+        again = paged_decode_attention(q, cache, ids, list(kept), 0)
+    clear_metadata_cache(cache)
+    fresh = paged_decode_attention(q, cache, ids, kept, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(again, first) and torch.equal(fresh, first)
