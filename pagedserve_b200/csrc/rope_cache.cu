@@ -15,8 +15,8 @@
 // and the pool bytes are bit-identical to the reference's (for bf16/f16 the
 // kernel uses paired 16-bit multiplies and adds, which round identically; see
 // Pair below).  A thread rotates one VEC-element piece of each half of one
-// head (the two halves meet in the rotation), 16-byte accesses when rows
-// allow.
+// head (the two halves meet in the rotation), or of two heads of one role,
+// 16-byte accesses when rows allow.
 #include <algorithm>
 #include <type_traits>
 
@@ -218,6 +218,107 @@ __global__ void __launch_bounds__(256) rope_cache_kernel(const RopeParams p) {
   }
 }
 
+// Two heads of one role (q, k or v) per unit: the same piece of heads 2m and
+// 2m + 1 of one token, both heads' loads issued before any arithmetic and
+// the token's cos/sin pieces loaded once for the two (64 bytes of q/k/v in
+// flight per thread instead of 32 at the same occupancy: 19.3 -> 18.0-18.8 us
+// on a 16 K-token pack).  Used when the q and kv head counts are both even,
+// so that no pair straddles two roles.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) rope_pair_kernel(const RopeParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int half = p.head_dim / 2;
+  const int pieces = half / VEC;
+  const int pairs = (p.hq + 2 * p.hkv) / 2;
+  const int per_tok = pairs * pieces;
+  const int64_t total = static_cast<int64_t>(per_tok) * p.tokens;
+  const int64_t hb = static_cast<int64_t>(half) * sizeof(T);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / per_tok;
+    const int r = static_cast<int>(i - t * per_tok);
+    const int pr = r / pieces;
+    const int64_t e0 = static_cast<int64_t>(r - pr * pieces) * VEC * sizeof(T);
+    const int hs = 2 * pr;  // first head of the pair (both of one role: the host checks even head counts)
+    const bool is_q = hs < p.hq, is_k = !is_q && hs < p.hq + p.hkv;
+    const int h = is_q ? hs : (is_k ? hs - p.hq : hs - p.hq - p.hkv);
+    const char* src = is_q ? p.q + t * p.qst + h * p.qsh + e0
+                           : (is_k ? p.k + t * p.kst + h * p.ksh + e0 : p.v + t * p.vst + h * p.vsh + e0);
+    const int64_t hst = is_q ? p.qsh : (is_k ? p.ksh : p.vsh);
+    Piece<T, VEC> xa1, xa2, xb1, xb2;
+    xa1.load(src);
+    xa2.load(src + hb);
+    xb1.load(src + hst);
+    xb2.load(src + hst + hb);
+    int64_t dst = -1;  // pool row of head h (head h + 1's row is block_size * head_dim elements on)
+    if (!is_q) {
+      const int64_t sl = __ldg(p.slots + t);
+      if (sl >= p.pool_slots) {
+        if (is_k && h == 0 && e0 == 0) flag_error(p.err, PSB_DEVERR_SLOT_RANGE);
+      } else if (sl >= 0) {
+        const int64_t blk = sl / p.block_size, off = sl - blk * p.block_size;
+        dst = (((p.layer_base_tiles + blk * p.hkv + h) * p.block_size + off) * p.head_dim) * sizeof(T) + e0;
+      }
+    }
+    const int64_t pool_head = static_cast<int64_t>(p.block_size) * p.head_dim * sizeof(T);
+    if (!is_q && !is_k) {
+      if (dst < 0) continue;
+      xa1.store(p.vc + dst);
+      xa2.store(p.vc + dst + hb);
+      xb1.store(p.vc + dst + pool_head);
+      xb2.store(p.vc + dst + pool_head + hb);
+      continue;
+    }
+    Piece<T, VEC> c1, c2, s1, s2;
+    const char* cs = p.cos + t * p.cst + e0;
+    const char* sn = p.sin + t * p.cst + e0;
+    c1.load(cs);
+    c2.load(cs + hb);
+    s1.load(sn);
+    s2.load(sn + hb);
+    Piece<T, VEC> oa1, oa2, ob1, ob2;
+    rotate<T, VEC>(xa1, xa2, c1, c2, s1, s2, oa1, oa2);
+    rotate<T, VEC>(xb1, xb2, c1, c2, s1, s2, ob1, ob2);
+    if (is_q) {
+      char* out = p.qo + t * p.qost + h * p.qosh + e0;
+      oa1.store(out);
+      oa2.store(out + hb);
+      ob1.store(out + p.qosh);
+      ob2.store(out + p.qosh + hb);
+      continue;
+    }
+    if (p.ko != nullptr) {
+      char* out = p.ko + t * p.kost + h * p.kosh + e0;
+      oa1.store(out);
+      oa2.store(out + hb);
+      ob1.store(out + p.kosh);
+      ob2.store(out + p.kosh + hb);
+    }
+    if (dst >= 0) {
+      oa1.store(p.kc + dst);
+      oa2.store(p.kc + dst + hb);
+      ob1.store(p.kc + dst + pool_head);
+      ob2.store(p.kc + dst + pool_head + hb);
+    }
+  }
+}
+
+template <typename T, int VEC>
+int launch_rope_pair(const RopeParams& p, cudaStream_t s, int sms) {
+  const auto kern = rope_pair_kernel<T, VEC>;
+  int occ = 0;
+  if (!kernel_occupancy(reinterpret_cast<const void*>(kern), 256, 0, &occ)) return PSB_ERR_CUDA;
+  if (!prefer_max_l1(reinterpret_cast<const void*>(kern))) return PSB_ERR_CUDA;
+  const int64_t units = static_cast<int64_t>(p.tokens) * ((p.hq + 2 * p.hkv) / 2) * (p.head_dim / 2 / VEC);
+  const int64_t blocks =
+      std::max<int64_t>(1, std::min<int64_t>((units + 255) / 256, static_cast<int64_t>(sms) * std::min(std::max(occ, 1), 8)));
+  discard_stale_error();
+  const cudaError_t e = launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, p);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  return check_launch();
+}
+
 template <typename T, int VEC>
 int launch_rope(const RopeParams& p, cudaStream_t s, int sms) {
   const int64_t units = static_cast<int64_t>(p.tokens) * (p.hq + 2 * p.hkv) * (p.head_dim / 2 / VEC);
@@ -306,6 +407,13 @@ extern "C" int psb_rope_reshape_and_cache(const void* query, int64_t q_stride_t,
           p.qost % 16 == 0 && p.qosh % 16 == 0;
   if (key_out != nullptr) vec = vec && aligned16(key_out) && p.kost % 16 == 0 && p.kosh % 16 == 0;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vec && num_q_heads % 2 == 0 && num_kv_heads % 2 == 0) {
+    switch (dtype) {
+      case PSB_BF16: return launch_rope_pair<__nv_bfloat16, 8>(p, s, sms);
+      case PSB_F16: return launch_rope_pair<__half, 8>(p, s, sms);
+      default: return launch_rope_pair<float, 4>(p, s, sms);
+    }
+  }
   switch (dtype) {
     case PSB_BF16: return vec ? launch_rope<__nv_bfloat16, 8>(p, s, sms) : launch_rope<__nv_bfloat16, 1>(p, s, sms);
     case PSB_F16: return vec ? launch_rope<__half, 8>(p, s, sms) : launch_rope<__half, 1>(p, s, sms);
