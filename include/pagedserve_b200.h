@@ -37,7 +37,7 @@ enum {
   PSB_OK = 0,
   PSB_ERR_INVALID = -1,     /* bad shape, stride, pointer or size argument */
   PSB_ERR_WORKSPACE = -2,   /* workspace smaller than *_workspace_size() */
-  PSB_ERR_UNSUPPORTED = -3, /* geometry/dtype this build has no kernel for */
+  PSB_ERR_UNSUPPORTED = -3, /* geometry/dtype the library has no kernel for */
   PSB_ERR_CUDA = -4         /* a CUDA runtime/driver call failed (see psb_last_cuda_error) */
 };
 
